@@ -1,0 +1,592 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config c2|c4]
+
+Headline workload (config 2 of the benchmark plan, per GPU): batched paged
+decode of Qwen3-0.6B attention -- B=64 requests, 16 q / 8 kv heads, head_dim
+128, context lengths uniform in [128, 4096], 16-token pages placed by a random
+permutation in a 32768-block pool, Q/K RMS-normed and RoPE'd at theta 1e6.
+A step is one decode step of the whole 28-layer attention stack: for every
+layer, the KV write of the new token (scatter) and the split-K decode, through
+the reference-named API ``triton_paged_attention_decode_batch``.
+
+``value`` = algorithmic bytes of all ranks' steps / max-over-ranks device time
+(GB/s); inputs resident in HBM; the KV read per step (~15.5 GB) is far larger
+than L2 (126 MB), so no flush is needed between steps.  ``e2e`` repeats the
+step through the same public API with the step's q/k/v copied from pinned
+host memory and the outputs copied back inside the timed region.
+``roofline`` is for the decode kernels (split + merge) timed live with CUDA
+events around every decode call of the timed region.
+
+Multi-GPU: one process per GPU (torchrun), each rank owns its own requests,
+pool and block table -- no collective on the data path ("scaling": "weak").
+``--config c4``: config 4 (Qwen3-8B heads 32/8, B=512 log-uniform [256,32768]),
+the 512 requests sharded over the ranks by LPT on length ("scaling": "strong").
+
+``--impl reference``: the reference's own algorithm (the CPU oracle port of
+qwen3/paged_attention.py:paged_attention) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+HEAD_DIM = 128
+BLOCK = 16
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+# ---------------------------------------------------------------------------
+# workloads (shapes only; data generated on the device)
+# ---------------------------------------------------------------------------
+
+def workload(config: str, rank: int, world: int):
+    if config == "c2":
+        rng = np.random.default_rng(1234 + rank)
+        lens = rng.integers(128, 4096, size=64, endpoint=True)
+        return dict(name="c2_paged_decode_qwen3_0.6b", H=16, Hkv=8, lens=lens, layers=28,
+                    num_blocks=32768, max_seq_len=4096, scaling="weak", batch_per_gpu=64)
+    if config == "c4":
+        rng = np.random.default_rng(4321)
+        all_lens = np.exp(rng.uniform(np.log(256), np.log(32768), size=512)).astype(np.int64)
+        from qwen3_engine_from_scratch_b200.dist import decode_cost, lpt_partition
+        shards = lpt_partition(decode_cost(all_lens), world)
+        lens = all_lens[shards[rank]]
+        blocks = int(sum((int(L) + BLOCK - 1) // BLOCK for L in lens)) + 64
+        return dict(name="c4_paged_decode_qwen3_8b_sharded", H=32, Hkv=8, lens=lens, layers=1,
+                    num_blocks=blocks, max_seq_len=32768, scaling="strong", batch_total=512,
+                    all_lens=all_lens)
+    raise SystemExit(f"unknown config {config}")
+
+
+def decode_bytes(lens, H, Hkv, D=HEAD_DIM, elem=2):
+    lens = np.asarray(lens, dtype=np.int64)
+    B = len(lens)
+    kv = int(lens.sum()) * Hkv * D * elem * 2
+    qo = B * H * D * elem * 2
+    tables = int(((lens + BLOCK - 1) // BLOCK).sum()) * 4
+    return kv + qo + tables + B * 8
+
+
+def scatter_bytes(B, Hkv, D=HEAD_DIM, elem=2):
+    return B * Hkv * D * elem * 2 * 2 + B * 12   # read + write K and V, row/len/table reads
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML sampled in a thread during the timed region)
+# ---------------------------------------------------------------------------
+
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+           0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+           0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+           0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, torch_device_index: int, period_s: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_device_index)
+            handle = None
+            bus = getattr(props, "pci_bus_id", None)
+            if bus is not None:
+                dom = getattr(props, "pci_domain_id", 0)
+                devid = getattr(props, "pci_device_id", 0)
+                try:
+                    handle = pynvml.nvmlDeviceGetHandleByPciBusId(
+                        f"{dom:08x}:{bus:02x}:{devid:02x}.0".encode())
+                except Exception:
+                    handle = None
+            if handle is None:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(torch_device_index)
+            self._nv = pynvml
+            self._h = handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report what we could not sample
+            self.error = repr(e)
+            self._nv = None
+        self.period = period_s
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append(mhz)
+                self.reasons |= int(r)
+            except Exception as e:
+                self.error = repr(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        reasons = [name for bit, name in REASONS.items() if self.reasons & bit and bit != 0x1]
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+               "source": "nvml"}
+        if self.error:
+            out["error"] = self.error
+        return out
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+def build_decode_state(w, device, seed):
+    """Pool, block table, row slots and per-layer inputs on the device."""
+    import torch
+    import qwen3_engine_from_scratch_b200 as qb
+
+    H, Hkv, D, layers = w["H"], w["Hkv"], HEAD_DIM, w["layers"]
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    B = len(lens)
+    g = torch.Generator(device=device).manual_seed(seed)
+    pool = qb.KVCachePool(num_blocks=w["num_blocks"], num_layers=layers, block_size=BLOCK,
+                          num_kv_heads=Hkv, head_dim=D, device=device, dtype=torch.bfloat16,
+                          max_seq_len=w["max_seq_len"], max_requests=B + 1)
+    perm = torch.randperm(w["num_blocks"], generator=g, device=device).cpu().tolist()
+    pool.free_block_ids = perm
+    caches = []
+    for L in lens:
+        c = qb.PagedKVCache(pool)
+        c._ensure_pages(int(L))           # pages for the L-1 context tokens + this step's token
+        c.seq_len = int(L) - 1
+        caches.append(c)
+    pool.seq_lens[[c.row_id for c in caches]] = torch.tensor([int(L) - 1 for L in lens],
+                                                             dtype=torch.int32, device=device)
+    rows = torch.tensor([c.row_id for c in caches], dtype=torch.int32, device=device)
+    # K/V of the context: N(0,1), K RMS-normed + RoPE'd (theta 1e6); written per layer
+    pos = np.concatenate([np.arange(int(L) - 1) for L in lens])
+    slots = np.concatenate([np.asarray(c.block_table, np.int64)[np.arange(int(L) - 1) // BLOCK] * BLOCK
+                            + np.arange(int(L) - 1) % BLOCK for c, L in zip(caches, lens)])
+    pos_t = torch.from_numpy(pos).to(device).float()
+    slots_t = torch.from_numpy(slots).to(device)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+
+    def rope(x, p):
+        ang = p[:, None] * inv[None]
+        cos = torch.cat([ang, ang], -1).cos()[:, None]
+        sin = torch.cat([ang, ang], -1).sin()[:, None]
+        return x * cos + torch.cat([-x[..., D // 2:], x[..., :D // 2]], -1) * sin
+
+    def rms(x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    T = len(pos)
+    chunk = 1 << 16
+    for layer in range(layers):
+        for s0 in range(0, T, chunk):
+            s1 = min(T, s0 + chunk)
+            k = rope(rms(torch.randn(s1 - s0, Hkv, D, generator=g, device=device)), pos_t[s0:s1])
+            v = torch.randn(s1 - s0, Hkv, D, generator=g, device=device)
+            qb.kv_scatter_slots(k.to(torch.bfloat16), v.to(torch.bfloat16), pool.k_buffer,
+                                pool.v_buffer, slots_t[s0:s1], layer)
+    qpos = torch.from_numpy(lens - 1).to(device).float()
+    qs = rope(rms(torch.randn(layers * B, H, D, generator=g, device=device)), qpos.repeat(layers))
+    q = qs.view(layers, B, H, 1, D).to(torch.bfloat16)
+    knew = rope(rms(torch.randn(layers * B, Hkv, D, generator=g, device=device)), qpos.repeat(layers))
+    k_new = knew.view(layers, B, Hkv, 1, D).to(torch.bfloat16)
+    v_new = torch.randn(layers, B, Hkv, 1, D, generator=g, device=device).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    return dict(pool=pool, caches=caches, rows=rows, q=q, k_new=k_new, v_new=v_new, B=B)
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import qwen3_engine_from_scratch_b200 as qb
+    from qwen3_engine_from_scratch_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    w = workload(args.config, rank, world)
+    st = build_decode_state(w, device, seed=1000 + rank)
+    pool, caches, rows = st["pool"], st["caches"], st["rows"]
+    q, k_new, v_new, B = st["q"], st["k_new"], st["v_new"], st["B"]
+    H, Hkv, layers = w["H"], w["Hkv"], w["layers"]
+    scale = HEAD_DIM ** -0.5
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    max_pages = pool.block_table_2d.shape[1]
+    n_splits = math.ceil(max_pages / max(1, qb._native.load().b200_paged_decode_default_split(B, Hkv, max_pages)))
+    launches_per_layer = 2 + (1 if n_splits > 1 else 0)
+
+    def layer_call(l):
+        ops.kv_scatter_rows(k_new[l], v_new[l], pool.k_buffer, pool.v_buffer, pool.seq_lens,
+                            pool.block_table_2d, rows, l)
+        return ops.paged_decode(q[l, :, :, 0], pool.k_buffer[:, l], pool.v_buffer[:, l],
+                                pool.block_table_2d, pool.seq_lens, rows, scale)
+
+    stream = torch.cuda.current_stream()
+    # warm-up
+    for _ in range(args.warmup):
+        for l in range(layers):
+            layer_call(l)
+    torch.cuda.synchronize()
+    qb.check_device_status(device)
+
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * layers)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * layers)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start.record(stream)
+    i = 0
+    for _ in range(args.steps):
+        for l in range(layers):
+            ops.kv_scatter_rows(k_new[l], v_new[l], pool.k_buffer, pool.v_buffer, pool.seq_lens,
+                                pool.block_table_2d, rows, l)
+            ev_a[i].record(stream)
+            ops.paged_decode(q[l, :, :, 0], pool.k_buffer[:, l], pool.v_buffer[:, l],
+                             pool.block_table_2d, pool.seq_lens, rows, scale)
+            ev_b[i].record(stream)
+            i += 1
+    stop.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(stop)
+    decode_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / len(ev_a)
+    qb.check_device_status(device)
+
+    # ---- e2e: host q/k/v (pinned) -> device, the public batch API, outputs -> host
+    hq = q.cpu().pin_memory()
+    hk = k_new.cpu().pin_memory()
+    hv = v_new.cpu().pin_memory()
+    hout = torch.empty((layers, B, 1, H * HEAD_DIM), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new)
+    e2e_steps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        for l in range(layers):
+            o = qb.triton_paged_attention_decode_batch(dq[l], dk[l], dv[l], caches, l, scale, rows)
+            hout[l].copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
+    if world > 1:
+        dist.barrier()
+
+    step_bytes = layers * (decode_bytes(lens, H, Hkv) + scatter_bytes(B, Hkv))
+    dec_bytes = decode_bytes(lens, H, Hkv)
+    t = torch.tensor([ms, e2e_ms, float(step_bytes), decode_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        ms, e2e_ms = float(tmax[0]), float(tmax[1])
+        total_bytes_per_step = float(tsum[2])
+    else:
+        total_bytes_per_step = float(step_bytes)
+    if rank != 0:
+        return None
+
+    ms_per_step = ms / args.steps
+    value = total_bytes_per_step * args.steps / (ms / 1e3) / 1e9
+    peaks, peak_src = read_peaks()
+    achieved = dec_bytes / (decode_ms / 1e3) / 1e9
+    traffic = read_traffic("paged_decode_split_kernel")
+    tokens = (w.get("batch_total") or B * world)
+    line = {
+        "metric": "paged_decode_attention_hbm_bandwidth",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": w["scaling"],
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: N(0,1) q/k/v, q/k RMS-normed + RoPE theta 1e6, random page permutation",
+        "config": {"workload": w["name"], "heads": f"{H}/{Hkv}", "head_dim": HEAD_DIM,
+                   "batch_per_gpu": B, "layers_per_step": layers,
+                   "context": "U[128,4096]" if args.config == "c2" else "logU[256,32768]",
+                   "block_size": BLOCK, "pool_blocks": w["num_blocks"],
+                   "l2": "inputs larger than L2 (KV read per step %.1f GB)" % (
+                       layers * dec_bytes / 1e9),
+                   "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU"},
+        "tok_per_s": round(tokens / (ms_per_step / 1e3), 1),
+        "e2e": {"value": round(total_bytes_per_step / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4),
+                "tok_per_s": round(tokens / (e2e_ms / 1e3), 1),
+                "h2d_bytes_per_step": int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2),
+                "d2h_bytes_per_step": int(hout.numel() * 2),
+                "api": "triton_paged_attention_decode_batch (pinned host q/k/v in, host out)"},
+        "roofline": {"kernel": "paged_decode_split_kernel + paged_decode_merge_kernel",
+                     "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": peak_src, "avg_launch_us": round(decode_ms * 1e3, 2),
+                     "bytes_per_launch": dec_bytes,
+                     "traffic": traffic},
+        "gpu_launches": args.steps * layers * launches_per_layer,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_budget)
+    return line
+
+
+def read_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))}, \
+            "measured (MEASURED_PEAKS.json)"
+    except Exception:
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+                "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def read_traffic(kernel):
+    """dram bytes (read+write) per launch from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        return json.load(open(p)).get(kernel)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference algorithm
+# ---------------------------------------------------------------------------
+
+def _cpu_work(w, seed=7):
+    """A host copy of one layer of the workload (compact pool of the used pages)."""
+    from oracle import synth
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    H, Hkv, D = w["H"], w["Hkv"], HEAD_DIM
+    pages = (lens + BLOCK - 1) // BLOCK
+    n = int(pages.sum())
+    perm = synth.det_permutation(seed, n)
+    bt = np.full((len(lens), int(pages.max())), -1, np.int32)
+    o = 0
+    for b, p in enumerate(pages):
+        bt[b, :p] = perm[o:o + p]
+        o += p
+    rng = np.random.default_rng(seed)
+    kp = rng.standard_normal((n, Hkv, BLOCK, D), dtype=np.float32)
+    vp = rng.standard_normal((n, Hkv, BLOCK, D), dtype=np.float32)
+    q = rng.standard_normal((len(lens), H, D), dtype=np.float32)
+    seq = (lens - 1).astype(np.int32)
+    return q, kp, vp, bt, seq
+
+
+def _cpu_worker(args):
+    """Spawned worker: attach the shared pool and run the oracle on some requests."""
+    from multiprocessing import shared_memory
+    from oracle.attention import paged_decode
+    (names, shapes, idx) = args
+    shms = [shared_memory.SharedMemory(name=n) for n in names]
+    arrs = [np.ndarray(s, dtype=np.float32 if i < 3 else np.int32, buffer=m.buf)
+            for i, (m, s) in enumerate(zip(shms, shapes))]
+    q, kp, vp, bt, seq = arrs
+    t0 = time.perf_counter()
+    paged_decode(q[idx], kp, vp, bt[idx], seq[idx], np.arange(len(idx)), BLOCK, HEAD_DIM ** -0.5)
+    dt = time.perf_counter() - t0
+    for m in shms:
+        m.close()
+    return dt
+
+
+class CpuDecodePool:
+    """The oracle decode of one layer of the workload on ``procs`` spawned processes."""
+
+    def __init__(self, w, procs):
+        import multiprocessing as mp
+        from multiprocessing import shared_memory
+        self.w = w
+        arrays = _cpu_work(w)
+        self.shm = []
+        self.names, self.shapes = [], []
+        for a in arrays:
+            m = shared_memory.SharedMemory(create=True, size=max(1, a.nbytes))
+            np.ndarray(a.shape, dtype=a.dtype, buffer=m.buf)[...] = a
+            self.shm.append(m)
+            self.names.append(m.name)
+            self.shapes.append(a.shape)
+        self.procs = procs
+        self.pool = mp.get_context("spawn").Pool(procs) if procs > 1 else None
+
+    def run(self, idx):
+        parts = [idx[i::self.procs] for i in range(self.procs)] if self.pool else [idx]
+        parts = [p for p in parts if len(p)]
+        jobs = [(self.names, self.shapes, p) for p in parts]
+        t0 = time.perf_counter()
+        if self.pool is not None:
+            self.pool.map(_cpu_worker, jobs)
+        else:
+            for j in jobs:
+                _cpu_worker(j)
+        return time.perf_counter() - t0
+
+    def close(self):
+        if self.pool is not None:
+            self.pool.close()
+            self.pool.join()
+        for m in self.shm:
+            m.close()
+            m.unlink()
+
+
+def cpu_baseline(w, budget_s=20.0, procs=1):
+    """Oracle port timed on the host: one layer of the batch, requests in order
+    until about ``budget_s`` seconds of CPU work."""
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    H, Hkv = w["H"], w["Hkv"]
+    cp = CpuDecodePool(w, procs)
+    try:
+        idx = np.arange(len(lens))
+        dt = cp.run(idx[:1])                       # warm-up / calibration on one request
+        per_req = max(dt, 1e-3)
+        n = int(min(len(lens), max(1, budget_s / per_req * procs)))
+        dt = cp.run(idx[:n])
+    finally:
+        cp.close()
+    b = decode_bytes(lens[:n], H, Hkv)
+    return {"value": round(b / dt / 1e9, 3), "unit": "GB/s", "cores": procs, "kind": "port",
+            "sample": f"1 layer x {n}/{len(lens)} requests of the workload ({dt:.2f} s), "
+                      f"oracle.paged_decode (numpy fp32 restatement of qwen3/paged_attention.py)"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+    if rank != 0:
+        return None
+    w = workload(args.config, 0, 1)
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    H, Hkv = w["H"], w["Hkv"]
+    procs = max(1, os.cpu_count() or 1)
+    cp = CpuDecodePool(w, procs)
+    try:
+        idx = np.arange(len(lens))
+        dt1 = cp.run(idx[: min(len(idx), procs)])
+        # size each step's sample so the whole run stays within ~3 minutes
+        per_req = dt1 / max(1, min(len(idx), procs)) * procs
+        budget_step = 150.0 / max(1, args.steps + args.warmup)
+        n = int(max(1, min(len(idx), budget_step / max(per_req / procs, 1e-4))))
+        sample = idx[:n]
+        for _ in range(args.warmup):
+            cp.run(sample)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cp.run(sample)
+        dt = time.perf_counter() - t0
+    finally:
+        cp.close()
+    b = decode_bytes(lens[:n], H, Hkv)
+    value = b * args.steps / dt / 1e9
+    line = {
+        "metric": "paged_decode_attention_hbm_bandwidth", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": w["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": w["name"], "heads": f"{H}/{Hkv}", "head_dim": HEAD_DIM,
+                   "batch_per_gpu": len(lens), "layers_per_step": 1},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": procs, "kind": "port",
+                         "sample": f"1 layer x {n}/{len(lens)} requests per step, oracle.paged_decode "
+                                   f"(numpy restatement of qwen3/paged_attention.py) on {procs} "
+                                   f"spawned processes"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from qwen3_engine_from_scratch_b200.dist import rank_env
+    rank, world, local_rank = rank_env()
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_b200(args, rank, world, local_rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

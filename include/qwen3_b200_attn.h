@@ -1,0 +1,174 @@
+/*
+ * qwen3_b200_attn.h -- C ABI of the B200 (sm_100a) attention hot path for the
+ * Qwen3 inference engine (uphome/Qwen3-engine-from-scratch).
+ *
+ * Three operations, each a hand-written CUDA kernel behind a plain-C entry
+ * point: raw device pointers, element strides, sizes, a CUDA stream.  No torch
+ * types cross this boundary.  All entry points only enqueue work on `stream`
+ * (no host synchronisation, no allocation, grid sizes derived from shapes
+ * only), so they can be captured in a CUDA graph.
+ *
+ * Conventions
+ *   - bf16 tensors are passed as `const void*` / `void*` (2-byte elements).
+ *   - Strides are in ELEMENTS (like torch.Tensor.stride()), int64.
+ *   - The innermost (head_dim) stride must be 1.
+ *   - The KV pool has the reference layout
+ *       (num_blocks, num_layers, num_kv_heads, block_size, head_dim)
+ *     (qwen3/PagedKVcache.py:50-53); block_size must be 16, head_dim 128.
+ *   - `dev_status` (nullable) points to one int32 in device memory; kernels
+ *     OR B200_DEV_* bits into it when they meet an out-of-range index (the
+ *     offending access is skipped, never performed).  Read it back with a
+ *     plain device-to-host copy when convenient.
+ *   - Return value: B200_OK (0) or a negative b200_status; nothing is
+ *     launched when an argument check fails.  No entry point aborts/exits.
+ */
+#ifndef QWEN3_B200_ATTN_H
+#define QWEN3_B200_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B200_OK = 0,
+  B200_ERR_INVALID_ARGUMENT = -1, /* null pointer, bad size or stride       */
+  B200_ERR_UNSUPPORTED = -2,      /* head_dim / block_size / GQA group size  */
+  B200_ERR_ALIGNMENT = -3,        /* pointer or stride not 16-byte aligned   */
+  B200_ERR_WORKSPACE = -4,        /* workspace missing or too small          */
+  B200_ERR_CUDA = -5,             /* launch / driver error                   */
+  B200_ERR_TENSOR_MAP = -6        /* TMA descriptor could not be encoded     */
+} b200_status;
+
+/* Bits OR-ed into *dev_status by the kernels. */
+#define B200_DEV_BAD_ROW 0x1      /* row_ids[b] outside [0, max_requests)       */
+#define B200_DEV_BAD_PAGE 0x2     /* block-table entry outside [0, num_blocks)  */
+#define B200_DEV_BAD_SLOT 0x4     /* slot_mapping entry past the pool           */
+#define B200_DEV_SEQ_OVERFLOW 0x8 /* position needs a page past max_pages       */
+#define B200_DEV_TIMEOUT 0x10     /* a bounded pipeline wait gave up            */
+
+/* Human-readable text for a b200_status value. */
+const char* b200_status_string(int status);
+
+/* ABI version of this library (major*100 + minor). */
+int b200_abi_version(void);
+
+/* Number of SMs of the current device (cached per device); <0 on error. */
+int b200_device_sm_count(void);
+
+/*
+ * KV-cache write, row addressed.  For request b (0 <= b < batch) and token s
+ * (0 <= s < n_tokens), head h:
+ *     row  = row_ids[b];  pos = seq_lens[row] + s;
+ *     phys = block_table[row * bt_stride_row + pos / 16];  off = pos % 16;
+ *     k_pool[phys, layer, h, off, :] = k_new[b, h, s, :]   (same for v)
+ * n_tokens == 1 replaces update_kv_batch_triton
+ *   (qwen3/kernels/paged_attention.py:353-377, kernel :292-350) as called by
+ *   KVCachePool.update_kv_batch (qwen3/PagedKVcache.py:99-114);
+ * n_tokens  > 1 replaces the per-request prefill write of
+ *   PagedKVCache.update (qwen3/PagedKVcache.py:187-214, called per request at
+ *   qwen3/attention.py:160-161) for a whole right-padded batch in one launch.
+ * k_new/v_new strides: (batch, head, token), head_dim stride 1.
+ * Pool strides: (block, layer, head, slot), head_dim stride 1.
+ */
+int b200_kv_scatter_rows(const void* k_new, const void* v_new,
+                         int64_t kn_stride_b, int64_t kn_stride_h, int64_t kn_stride_s,
+                         int64_t vn_stride_b, int64_t vn_stride_h, int64_t vn_stride_s,
+                         void* k_pool, void* v_pool,
+                         int64_t kp_stride_blk, int64_t kp_stride_layer,
+                         int64_t kp_stride_h, int64_t kp_stride_slot,
+                         int64_t vp_stride_blk, int64_t vp_stride_layer,
+                         int64_t vp_stride_h, int64_t vp_stride_slot,
+                         const int32_t* seq_lens, const int32_t* block_table,
+                         int64_t bt_stride_row, const int32_t* row_ids,
+                         int batch, int n_tokens, int num_kv_heads, int head_dim,
+                         int block_size, int num_blocks, int max_pages, int max_requests,
+                         int layer, int32_t* dev_status, void* stream);
+
+/*
+ * KV-cache write, slot addressed (vLLM store_kvcache convention).  Token t:
+ *     slot = slot_mapping[t]; if slot < 0: skip;
+ *     k_pool[slot / 16, layer, h, slot % 16, :] = k[t, h, :]   (same for v)
+ * The same pool addressing as PagedKVCache.update (qwen3/PagedKVcache.py:198-214)
+ * with (phys, off) flattened; used by packed varlen prefill.
+ * slot_mapping is int32 (slot_is_int64 == 0) or int64 (slot_is_int64 != 0).
+ */
+int b200_kv_scatter_slots(const void* k, const void* v,
+                          int64_t k_stride_t, int64_t k_stride_h,
+                          int64_t v_stride_t, int64_t v_stride_h,
+                          void* k_pool, void* v_pool,
+                          int64_t kp_stride_blk, int64_t kp_stride_layer,
+                          int64_t kp_stride_h, int64_t kp_stride_slot,
+                          int64_t vp_stride_blk, int64_t vp_stride_layer,
+                          int64_t vp_stride_h, int64_t vp_stride_slot,
+                          const void* slot_mapping, int slot_is_int64,
+                          int n_tokens, int num_kv_heads, int head_dim, int block_size,
+                          int num_blocks, int layer, int32_t* dev_status, void* stream);
+
+/*
+ * Split-K paged decode: workspace bytes needed for `batch` requests, `num_heads`
+ * query heads and a block table `max_pages` wide, with `pages_per_split`
+ * pages per split (<= 0 selects the library default).  Depends on shapes only.
+ */
+size_t b200_paged_decode_workspace_size(int batch, int num_heads, int max_pages,
+                                        int pages_per_split);
+
+/* The split size the library picks for these shapes when pages_per_split <= 0. */
+int b200_paged_decode_default_split(int batch, int num_kv_heads, int max_pages);
+
+/*
+ * Paged decode attention (flash-decoding).  For request b, query head h:
+ *     row = row_ids[b];  L = seq_lens[row] + 1;
+ *     out[b,h,:] = softmax_j(scale * q[b,h,:].k_j) . v_j  over tokens j < L,
+ * token j of the request at page block_table[row, j/16], slot j%16, kv head
+ * h / (num_heads/num_kv_heads).  Replaces paged_attn_decode_kernel and
+ * paged_attention_decode_triton (qwen3/kernels/paged_attention.py:27-178).
+ * k_pool/v_pool point at the layer's first element (pool + layer*stride_layer),
+ * strides (block, head, slot) in elements, head_dim stride 1.
+ * q strides (batch, head); out strides (batch, head).  fp32 softmax, bf16 out.
+ * `workspace` must hold b200_paged_decode_workspace_size(...) bytes (16-byte
+ * aligned); it carries the per-split partials between the two kernels.
+ */
+int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                      const void* k_pool, const void* v_pool,
+                      int64_t kv_stride_blk, int64_t kv_stride_h, int64_t kv_stride_slot,
+                      const int32_t* block_table, int64_t bt_stride_row,
+                      const int32_t* seq_lens, const int32_t* row_ids,
+                      void* out, int64_t out_stride_b, int64_t out_stride_h,
+                      int batch, int num_heads, int num_kv_heads, int head_dim,
+                      int block_size, int num_blocks, int max_pages, int max_requests,
+                      float scale, int pages_per_split,
+                      void* workspace, size_t workspace_bytes,
+                      int32_t* dev_status, void* stream);
+
+/*
+ * Varlen causal prefill attention.  Sequence i owns rows
+ * [cu_seqlens[i], cu_seqlens[i] + len_i) of the packed q/k/v/out tensors, with
+ * len_i = cu_seqlens[i+1] - cu_seqlens[i] when seq_lens_opt is NULL (packed
+ * varlen) or len_i = seq_lens_opt[i] (right-padded batch: cu_seqlens[i] =
+ * i * S).  Query row m attends keys n <= m of its own sequence; q head h reads
+ * kv head h / (num_heads/num_kv_heads); fp32 online softmax, bf16 output.
+ * Replaces flash_attention_varlen_kernel / flash_attention_prefill
+ * (qwen3/kernels/flash_attention_varlen.py:25-194) without its host sync:
+ * `max_seqlen` (>= every len_i) sizes the grid.  With zero_pad_rows != 0 the
+ * rows [cu_seqlens[i] + len_i, cu_seqlens[i] + max_seqlen) of `out` are set to
+ * zero, as the padded-batch adapter does (flash_attention_varlen.py:255-257).
+ * q (T, H, D), k/v (T, Hkv, D): token and head strides in elements, head_dim
+ * stride 1; out (T, H, D) with strides (token, head).  head_dim must be 128.
+ */
+int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                        const void* k, int64_t k_stride_t, int64_t k_stride_h,
+                        const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                        void* out, int64_t o_stride_t, int64_t o_stride_h,
+                        const int32_t* cu_seqlens, const int32_t* seq_lens_opt,
+                        int num_seqs, int total_tokens, int max_seqlen,
+                        int num_heads, int num_kv_heads, int head_dim,
+                        float scale, int zero_pad_rows, int32_t* dev_status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN3_B200_ATTN_H */

@@ -1,0 +1,33 @@
+"""B200-native (sm_100a) attention hot path for the Qwen3 inference engine.
+
+Hand-written CUDA kernels behind the C ABI in ``include/qwen3_b200_attn.h``:
+
+* paged decode attention (split-K flash-decoding, TMA-staged pages, mma.sync
+  with the GQA heads on the N side, separate merge kernel);
+* varlen causal prefill attention;
+* KV-cache slot scatter (row-addressed and slot_mapping-addressed).
+
+``ops`` holds the reference-facing functions (same names and arguments as the
+reference engine's kernel wrappers), ``paged_kv`` the host-side pool / request
+handles, ``shim`` the drop-in binding into the reference engine, and
+``dist`` the multi-GPU request sharding.
+"""
+
+from .ops import (  # noqa: F401
+    paged_attention_decode_triton,
+    triton_paged_attention_decode,
+    triton_paged_attention_decode_batch,
+    update_kv_batch_triton,
+    flash_attention_prefill,
+    flash_attention_prefill_batched,
+    paged_decode,
+    kv_scatter_rows,
+    kv_scatter_slots,
+    device_status,
+    clear_device_status,
+    check_device_status,
+    decode_workspace_bytes,
+)
+from .paged_kv import KVCachePool, PagedKVCache  # noqa: F401
+
+__version__ = "0.1.0"

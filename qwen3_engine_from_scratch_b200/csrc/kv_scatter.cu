@@ -1,0 +1,215 @@
+// KV-cache slot scatter: copy new K/V rows (head_dim bf16 = 256 bytes each)
+// into the paged pool.  HBM-bound byte movement; one thread moves one 16-byte
+// chunk of K and the matching chunk of V, so a warp writes two full 256-byte
+// rows of each tensor with 16-byte vector stores.
+//
+//   rows  mode: position = seq_lens[row_ids[b]] + s, page from the 2-D block
+//               table (update_kv_batch_kernel, qwen3/kernels/paged_attention.py:
+//               292-350, and PagedKVCache.update, qwen3/PagedKVcache.py:187-214)
+//   slots mode: slot = slot_mapping[t] = phys * block_size + offset
+//
+// Every index is range-checked; an out-of-range index sets a dev_status bit
+// and the row is skipped (never written out of bounds).
+#include "common.cuh"
+
+namespace {
+
+constexpr int kChunksPerRow = 16;  // 128 bf16 = 256 bytes = 16 x 16 B
+constexpr int kThreads = 256;
+
+B200_DEVICE uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+struct RowsArgs {
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  int64_t kn_b, kn_h, kn_s, vn_b, vn_h, vn_s;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  int64_t kp_blk, kp_layer, kp_h, kp_slot, vp_blk, vp_layer, vp_h, vp_slot;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int64_t bt_row;
+  const int32_t* row_ids;
+  int batch, n_tokens, num_kv_heads, block_size, num_blocks, max_pages, max_requests, layer;
+  int32_t* dev_status;
+};
+
+__global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArgs a) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int chunk = static_cast<int>(idx & (kChunksPerRow - 1));
+  int64_t r = idx >> 4;  // (b, s, h) row index
+  const int64_t total = static_cast<int64_t>(a.batch) * a.n_tokens * a.num_kv_heads;
+  if (r >= total) return;
+  const int h = static_cast<int>(r % a.num_kv_heads);
+  r /= a.num_kv_heads;
+  const int s = static_cast<int>(r % a.n_tokens);
+  const int b = static_cast<int>(r / a.n_tokens);
+
+  const int row = a.row_ids[b];
+  if (row < 0 || row >= a.max_requests) {
+    if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_ROW);
+    return;
+  }
+  const int64_t pos = static_cast<int64_t>(a.seq_lens[row]) + s;
+  const int64_t page = pos / a.block_size;
+  if (pos < 0 || page >= a.max_pages) {
+    if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
+    return;
+  }
+  const int phys = a.block_table[row * a.bt_row + page];
+  if (phys < 0 || phys >= a.num_blocks) {
+    if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
+    return;
+  }
+  const int64_t off = pos - page * a.block_size;
+  const int64_t e = static_cast<int64_t>(chunk) * 8;
+
+  const uint4 kv = ld_stream(a.k_new + b * a.kn_b + h * a.kn_h + s * a.kn_s + e);
+  const uint4 vv = ld_stream(a.v_new + b * a.vn_b + h * a.vn_h + s * a.vn_s + e);
+  *reinterpret_cast<uint4*>(a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
+                            off * a.kp_slot + e) = kv;
+  *reinterpret_cast<uint4*>(a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
+                            off * a.vp_slot + e) = vv;
+}
+
+struct SlotsArgs {
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t k_t, k_h, v_t, v_h;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  int64_t kp_blk, kp_layer, kp_h, kp_slot, vp_blk, vp_layer, vp_h, vp_slot;
+  const void* slots;
+  int slot_is_int64;
+  int n_tokens, num_kv_heads, block_size, num_blocks, layer;
+  int32_t* dev_status;
+};
+
+__global__ void __launch_bounds__(kThreads) kv_scatter_slots_kernel(const SlotsArgs a) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int chunk = static_cast<int>(idx & (kChunksPerRow - 1));
+  int64_t r = idx >> 4;  // (t, h) row index
+  if (r >= static_cast<int64_t>(a.n_tokens) * a.num_kv_heads) return;
+  const int h = static_cast<int>(r % a.num_kv_heads);
+  const int64_t t = r / a.num_kv_heads;
+  const int64_t slot = a.slot_is_int64 ? static_cast<const int64_t*>(a.slots)[t]
+                                       : static_cast<int64_t>(static_cast<const int32_t*>(a.slots)[t]);
+  if (slot < 0) return;  // padding token
+  const int64_t phys = slot / a.block_size;
+  if (phys >= a.num_blocks) {
+    if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_SLOT);
+    return;
+  }
+  const int64_t off = slot - phys * a.block_size;
+  const int64_t e = static_cast<int64_t>(chunk) * 8;
+  const uint4 kv = ld_stream(a.k + t * a.k_t + h * a.k_h + e);
+  const uint4 vv = ld_stream(a.v + t * a.v_t + h * a.v_h + e);
+  *reinterpret_cast<uint4*>(a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
+                            off * a.kp_slot + e) = kv;
+  *reinterpret_cast<uint4*>(a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
+                            off * a.vp_slot + e) = vv;
+}
+
+bool mult8(int64_t s) { return (s & 7) == 0; }
+
+}  // namespace
+
+extern "C" int b200_kv_scatter_rows(
+    const void* k_new, const void* v_new, int64_t kn_stride_b, int64_t kn_stride_h,
+    int64_t kn_stride_s, int64_t vn_stride_b, int64_t vn_stride_h, int64_t vn_stride_s,
+    void* k_pool, void* v_pool, int64_t kp_stride_blk, int64_t kp_stride_layer,
+    int64_t kp_stride_h, int64_t kp_stride_slot, int64_t vp_stride_blk, int64_t vp_stride_layer,
+    int64_t vp_stride_h, int64_t vp_stride_slot, const int32_t* seq_lens,
+    const int32_t* block_table, int64_t bt_stride_row, const int32_t* row_ids, int batch,
+    int n_tokens, int num_kv_heads, int head_dim, int block_size, int num_blocks, int max_pages,
+    int max_requests, int layer, int32_t* dev_status, void* stream) {
+  if (batch < 0 || n_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0 ||
+      max_pages <= 0 || max_requests <= 0 || layer < 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || n_tokens == 0) return B200_OK;
+  if (!k_new || !v_new || !k_pool || !v_pool || !seq_lens || !block_table || !row_ids)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return B200_ERR_UNSUPPORTED;
+  if (!b200host::aligned16(k_new) || !b200host::aligned16(v_new) ||
+      !b200host::aligned16(k_pool) || !b200host::aligned16(v_pool))
+    return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {kn_stride_b, kn_stride_h, kn_stride_s, vn_stride_b,
+                             vn_stride_h, vn_stride_s, kp_stride_blk, kp_stride_layer,
+                             kp_stride_h, kp_stride_slot, vp_stride_blk, vp_stride_layer,
+                             vp_stride_h, vp_stride_slot};
+  for (int64_t s : strides)
+    if (!mult8(s)) return B200_ERR_ALIGNMENT;
+
+  RowsArgs a;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.kn_b = kn_stride_b; a.kn_h = kn_stride_h; a.kn_s = kn_stride_s;
+  a.vn_b = vn_stride_b; a.vn_h = vn_stride_h; a.vn_s = vn_stride_s;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.kp_blk = kp_stride_blk; a.kp_layer = kp_stride_layer; a.kp_h = kp_stride_h;
+  a.kp_slot = kp_stride_slot;
+  a.vp_blk = vp_stride_blk; a.vp_layer = vp_stride_layer; a.vp_h = vp_stride_h;
+  a.vp_slot = vp_stride_slot;
+  a.seq_lens = seq_lens; a.block_table = block_table; a.bt_row = bt_stride_row;
+  a.row_ids = row_ids;
+  a.batch = batch; a.n_tokens = n_tokens; a.num_kv_heads = num_kv_heads;
+  a.block_size = block_size; a.num_blocks = num_blocks; a.max_pages = max_pages;
+  a.max_requests = max_requests; a.layer = layer; a.dev_status = dev_status;
+
+  const int64_t threads = static_cast<int64_t>(batch) * n_tokens * num_kv_heads * kChunksPerRow;
+  const int64_t blocks = (threads + kThreads - 1) / kThreads;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  kv_scatter_rows_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
+                           static_cast<cudaStream_t>(stream)>>>(a);
+  return b200host::status_from_cuda(cudaGetLastError());
+}
+
+extern "C" int b200_kv_scatter_slots(
+    const void* k, const void* v, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_t,
+    int64_t v_stride_h, void* k_pool, void* v_pool, int64_t kp_stride_blk,
+    int64_t kp_stride_layer, int64_t kp_stride_h, int64_t kp_stride_slot, int64_t vp_stride_blk,
+    int64_t vp_stride_layer, int64_t vp_stride_h, int64_t vp_stride_slot,
+    const void* slot_mapping, int slot_is_int64, int n_tokens, int num_kv_heads, int head_dim,
+    int block_size, int num_blocks, int layer, int32_t* dev_status, void* stream) {
+  if (n_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0 || layer < 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (n_tokens == 0) return B200_OK;
+  if (!k || !v || !k_pool || !v_pool || !slot_mapping) return B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return B200_ERR_UNSUPPORTED;
+  if (!b200host::aligned16(k) || !b200host::aligned16(v) || !b200host::aligned16(k_pool) ||
+      !b200host::aligned16(v_pool))
+    return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {k_stride_t, k_stride_h, v_stride_t, v_stride_h,
+                             kp_stride_blk, kp_stride_layer, kp_stride_h, kp_stride_slot,
+                             vp_stride_blk, vp_stride_layer, vp_stride_h, vp_stride_slot};
+  for (int64_t s : strides)
+    if (!mult8(s)) return B200_ERR_ALIGNMENT;
+
+  SlotsArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.k_t = k_stride_t; a.k_h = k_stride_h; a.v_t = v_stride_t; a.v_h = v_stride_h;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.kp_blk = kp_stride_blk; a.kp_layer = kp_stride_layer; a.kp_h = kp_stride_h;
+  a.kp_slot = kp_stride_slot;
+  a.vp_blk = vp_stride_blk; a.vp_layer = vp_stride_layer; a.vp_h = vp_stride_h;
+  a.vp_slot = vp_stride_slot;
+  a.slots = slot_mapping; a.slot_is_int64 = slot_is_int64;
+  a.n_tokens = n_tokens; a.num_kv_heads = num_kv_heads; a.block_size = block_size;
+  a.num_blocks = num_blocks; a.layer = layer; a.dev_status = dev_status;
+
+  const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kChunksPerRow;
+  const int64_t blocks = (threads + kThreads - 1) / kThreads;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  kv_scatter_slots_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(a);
+  return b200host::status_from_cuda(cudaGetLastError());
+}

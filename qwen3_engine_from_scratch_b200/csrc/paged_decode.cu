@@ -1,0 +1,506 @@
+// Paged decode attention for sm_100a: split-K flash-decoding over the paged
+// KV pool (the GPU-resident 2-D block table and row slots of
+// qwen3/PagedKVcache.py), replacing paged_attn_decode_kernel
+// (qwen3/kernels/paged_attention.py:27-129).
+//
+// Work decomposition
+//   grid.x = request b x kv head hkv ("pair"), grid.y = split index.  A split
+//   is `pages_per_split` consecutive 16-token pages of the pair's sequence;
+//   CTAs whose split starts past the sequence exit at once, so the grid
+//   depends on shapes only (CUDA-graph safe while seq_lens change).
+//   A CTA has 4 warps.  Warp w takes pages w, w+4, ... of the split and keeps
+//   its own online-softmax state; the 4 states are merged in shared memory at
+//   the end.  A pair with one split writes the bf16 output directly; else the
+//   split writes an fp32 partial (m, l, acc) and a second kernel merges them.
+//
+// Data movement
+//   Each page of one kv head is a contiguous 16 x 128 bf16 tile (4 KB) of K
+//   and one of V.  Lane 0 of a warp stages them into a per-warp ring of
+//   shared-memory slots with 4 TMA tensor loads (two 64-column boxes per
+//   tensor, 128-byte swizzle, L2 evict-first) that complete on the slot's
+//   mbarrier; all waits are bounded.
+//
+// Math (per page, per warp; G = num_heads / num_kv_heads <= 8)
+//   S^T (16 tokens x 8 heads) = K (16 x 128) . Q^T (128 x 8): 8 x mma.m16n8k16,
+//   tokens on the M side so the G query heads fill the N = 8 side (heads >= G
+//   are zero).  K fragments come from ldmatrix on the swizzled tile.
+//   Online softmax in base 2 on fp32 scores (max over the 16 tokens = 3 xor
+//   shuffles), P rounded to bf16, transposed in registers with movmatrix into
+//   the B operand of O^T (128 x 8) += V^T (128 x 16) . P (16 x 8): 8 more
+//   mma with V^T fragments from ldmatrix.trans.  The rescale factor of a head
+//   lives in the same lane as that head's accumulator columns, so no shuffle
+//   is needed for it.
+#include <math.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kD = 128;
+constexpr int kBS = 16;
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 3;
+constexpr int kPageBytes = kBS * kD * 2;  // 4096
+constexpr int kHalfBytes = kPageBytes / 2;
+constexpr int kSlotBytes = 2 * kPageBytes;
+constexpr int kMaxG = 8;
+constexpr int kAccStride = 132;  // floats per head row of the merge buffer
+constexpr int kDefaultPagesPerSplit = 16;
+constexpr int kMaxPagesPerSplit = 32 * kWarps;  // a warp's page ids live one per lane
+constexpr int kSmemBytes = kWarps * kStages * kSlotBytes + 1024;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;
+  int64_t q_b, q_h;
+  const int32_t* block_table;
+  int64_t bt_row;
+  const int32_t* seq_lens;
+  const int32_t* row_ids;
+  __nv_bfloat16* out;
+  int64_t o_b, o_h;
+  float* ws_acc;  // [batch][num_heads][max_splits][128]
+  float* ws_ml;   // [batch][num_heads][max_splits][2]
+  int batch, num_heads, num_kv_heads, group, num_blocks, max_pages, max_requests;
+  int pages_per_split, max_splits;
+  float scale_log2;
+  int32_t* dev_status;
+};
+
+// Visible pages of request b: L = seq_lens[row] + 1 tokens (the current token
+// was written by the scatter first), clamped to the block table.  Returns the
+// page count (0 for an invalid row) and sets L.
+B200_DEVICE int request_pages(const DecodeArgs& a, int b, int& row, int& L, int& err) {
+  err = 0;
+  row = a.row_ids[b];
+  if (row < 0 || row >= a.max_requests) {
+    err = B200_DEV_BAD_ROW;
+    L = 0;
+    return 0;
+  }
+  L = a.seq_lens[row] + 1;
+  if (L <= 0) {
+    err = B200_DEV_SEQ_OVERFLOW;
+    L = 0;
+    return 0;
+  }
+  int npages = (L + kBS - 1) / kBS;
+  if (npages > a.max_pages) {
+    err = B200_DEV_SEQ_OVERFLOW;
+    npages = a.max_pages;
+    L = npages * kBS;
+  }
+  return npages;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    paged_decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
+                              const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kWarps * kStages];
+  __shared__ float s_ml[kWarps][kMaxG][2];
+
+  const int pair = blockIdx.x;
+  const int split = blockIdx.y;
+  const int b = pair / a.num_kv_heads;
+  const int hkv = pair - b * a.num_kv_heads;
+  const int G = a.group;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int row, L, err;
+  const int npages = request_pages(a, b, row, L, err);
+  if (split == 0 && err != 0 && threadIdx.x == 0) b200::flag_error(a.dev_status, err);
+  if (npages == 0) {
+    // invalid row / empty sequence: split 0 writes zeros for this pair's heads
+    if (split == 0) {
+      for (int h = 0; h < G; ++h)
+        a.out[b * a.o_b + (hkv * G + h) * a.o_h + threadIdx.x] = __float2bfloat16(0.f);
+    }
+    return;
+  }
+  const int p_begin = split * a.pages_per_split;
+  if (p_begin >= npages) return;
+  const int p_end = min(npages, p_begin + a.pages_per_split);
+  const int nsplit = (npages + a.pages_per_split - 1) / a.pages_per_split;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem + warp * kStages * kSlotBytes;
+
+  if (threadIdx.x == 0) {
+    b200::prefetch_tensormap(&kmap);
+    b200::prefetch_tensormap(&vmap);
+    for (int i = 0; i < kWarps * kStages; ++i) b200::mbar_init(b200::smem_u32(&bars[i]), 1);
+    b200::fence_mbar_init();
+  }
+  __syncthreads();
+
+  // pages of this warp: p_begin + warp + kWarps * i, i < n_mine (<= 32)
+  const int first = p_begin + warp;
+  const int n_mine = first < p_end ? (p_end - first + kWarps - 1) / kWarps : 0;
+  int my_phys = 0;
+  if (lane < n_mine) {
+    const int p = first + kWarps * lane;
+    int ph = a.block_table[static_cast<int64_t>(row) * a.bt_row + p];
+    if (ph < 0 || ph >= a.num_blocks) {
+      b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
+      ph = 0;
+    }
+    my_phys = ph;
+  }
+
+  // Q^T fragments: lane (g, c) holds head g, dims 16ks + 2c (+1) and +8.
+  const int g = lane >> 2;
+  const int c = lane & 3;
+  uint32_t qb[8][2];
+  {
+    const bool qv = g < G;
+    const __nv_bfloat16* qrow = a.q + b * a.q_b + (hkv * G + (qv ? g : 0)) * a.q_h + 2 * c;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qb[ks][0] = qv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks) : 0u;
+      qb[ks][1] = qv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8) : 0u;
+    }
+  }
+
+  const uint64_t policy = b200::l2_policy_evict_first();
+  const uint32_t bar0 = b200::smem_u32(&bars[warp * kStages]);
+  const uint32_t ring_u32 = b200::smem_u32(ring);
+
+  auto issue = [&](int i, int slot) {
+    const int phys = __shfl_sync(0xffffffffu, my_phys, i);
+    if (lane == 0) {
+      const uint32_t bar = bar0 + 8 * slot;
+      const uint32_t dst = ring_u32 + slot * kSlotBytes;
+      b200::mbar_arrive_expect_tx(bar, kSlotBytes);
+      b200::tma_load_4d(dst, &kmap, bar, 0, 0, hkv, phys, policy);
+      b200::tma_load_4d(dst + kHalfBytes, &kmap, bar, 64, 0, hkv, phys, policy);
+      b200::tma_load_4d(dst + kPageBytes, &vmap, bar, 0, 0, hkv, phys, policy);
+      b200::tma_load_4d(dst + kPageBytes + kHalfBytes, &vmap, bar, 64, 0, hkv, phys, policy);
+    }
+  };
+
+  // per-lane ldmatrix address terms (128-byte swizzle: chunk ^= row & 7)
+  const int mi = lane >> 3;
+  const int sw = lane & 7;
+  const uint32_t k_row = static_cast<uint32_t>(((lane & 7) + ((mi & 1) << 3)) * 128);
+  const int k_chunk_hi = mi >> 1;
+  const uint32_t v_row = static_cast<uint32_t>(((lane & 7) + ((mi >> 1) << 3)) * 128);
+  const int v_chunk_lo = mi & 1;
+
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float acc[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+
+  int issued = 0;
+  for (; issued < n_mine && issued < kStages; ++issued) issue(issued, issued);
+
+  int consumed = 0;
+  bool timed_out = false;
+  for (; consumed < n_mine; ++consumed) {
+    const int slot = consumed % kStages;
+    const uint32_t parity = static_cast<uint32_t>((consumed / kStages) & 1);
+    const bool ok = b200::mbar_wait_bounded(bar0 + 8 * slot, parity);
+    if (__any_sync(0xffffffffu, !ok)) {
+      timed_out = true;
+      break;
+    }
+    const uint32_t kbase = ring_u32 + slot * kSlotBytes;
+    const uint32_t vbase = kbase + kPageBytes;
+
+    // ---- S^T = K . Q^T
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int chunk = ((ks & 3) << 1) + k_chunk_hi;
+      const uint32_t addr = kbase + (ks >> 2) * kHalfBytes + k_row + ((chunk ^ sw) << 4);
+      uint32_t a0, a1, a2, a3;
+      b200::ldmatrix_x4(addr, a0, a1, a2, a3);
+      b200::mma_bf16_16816(s, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+    }
+
+    // ---- online softmax (base 2); lane holds tokens g, g+8 x heads 2c, 2c+1
+    const int valid = L - (first + kWarps * consumed) * kBS;  // >= 1
+    float x0 = s[0] * a.scale_log2, x1 = s[1] * a.scale_log2;
+    float x2 = s[2] * a.scale_log2, x3 = s[3] * a.scale_log2;
+    if (g >= valid) x0 = x1 = -INFINITY;
+    if (g + 8 >= valid) x2 = x3 = -INFINITY;
+    float pm0 = fmaxf(x0, x2), pm1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, o));
+      pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, o));
+    }
+    const float mn0 = fmaxf(m0, pm0), mn1 = fmaxf(m1, pm1);
+    const float al0 = b200::ex2(m0 - mn0), al1 = b200::ex2(m1 - mn1);
+    const uint32_t plo = b200::pack_bf16x2(b200::ex2(x0 - mn0), b200::ex2(x1 - mn1));
+    const uint32_t phi = b200::pack_bf16x2(b200::ex2(x2 - mn0), b200::ex2(x3 - mn1));
+    l0 = l0 * al0 + (b200::bf16_lo(plo) + b200::bf16_lo(phi));
+    l1 = l1 * al1 + (b200::bf16_hi(plo) + b200::bf16_hi(phi));
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      acc[mt][0] *= al0;
+      acc[mt][1] *= al1;
+      acc[mt][2] *= al0;
+      acc[mt][3] *= al1;
+    }
+
+    // ---- O^T += V^T . P
+    const uint32_t pb0 = b200::movmatrix_trans(plo);
+    const uint32_t pb1 = b200::movmatrix_trans(phi);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int chunk = ((mt & 3) << 1) + v_chunk_lo;
+      const uint32_t addr = vbase + (mt >> 2) * kHalfBytes + v_row + ((chunk ^ sw) << 4);
+      uint32_t a0, a1, a2, a3;
+      b200::ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+      b200::mma_bf16_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+
+    __syncwarp();
+    if (issued < n_mine) {
+      issue(issued, slot);
+      ++issued;
+    }
+  }
+
+  if (timed_out) {
+    if (lane == 0) b200::flag_error(a.dev_status, B200_DEV_TIMEOUT);
+    // let the copies this warp still has in flight land before the CTA exits
+    for (int j = consumed; j < issued; ++j)
+      b200::mbar_wait_bounded(bar0 + 8 * (j % kStages), static_cast<uint32_t>((j / kStages) & 1));
+  }
+
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+
+  // ---- merge the 4 warp states (ring smem reused once every warp is done)
+  __syncthreads();
+  float* mbuf = reinterpret_cast<float*>(smem);
+  {
+    float* wbuf = mbuf + warp * kMaxG * kAccStride;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d = 16 * mt + g;
+      wbuf[(2 * c) * kAccStride + d] = acc[mt][0];
+      wbuf[(2 * c + 1) * kAccStride + d] = acc[mt][1];
+      wbuf[(2 * c) * kAccStride + d + 8] = acc[mt][2];
+      wbuf[(2 * c + 1) * kAccStride + d + 8] = acc[mt][3];
+    }
+    if (g == 0) {
+      s_ml[warp][2 * c][0] = m0;
+      s_ml[warp][2 * c][1] = l0;
+      s_ml[warp][2 * c + 1][0] = m1;
+      s_ml[warp][2 * c + 1][1] = l1;
+    }
+  }
+  __syncthreads();
+
+  const int d = threadIdx.x;
+  for (int h = 0; h < G; ++h) {
+    float mt = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mt = fmaxf(mt, s_ml[w][h][0]);
+    float o = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float sc = b200::ex2(s_ml[w][h][0] - mt);
+      o += sc * mbuf[(w * kMaxG + h) * kAccStride + d];
+      l += sc * s_ml[w][h][1];
+    }
+    const int hq = hkv * G + h;
+    if (nsplit == 1) {
+      a.out[b * a.o_b + hq * a.o_h + d] = __float2bfloat16(o / l);
+    } else {
+      const int64_t base = (static_cast<int64_t>(b) * a.num_heads + hq) * a.max_splits + split;
+      a.ws_acc[base * kD + d] = o;
+      if (d == 0) {
+        a.ws_ml[base * 2] = mt;
+        a.ws_ml[base * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+// One warp per (request, query head): merge the per-split partials.
+__global__ void __launch_bounds__(256) paged_decode_merge_kernel(const DecodeArgs a) {
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= static_cast<int64_t>(a.batch) * a.num_heads) return;
+  const int b = static_cast<int>(gw / a.num_heads);
+  const int hq = static_cast<int>(gw - static_cast<int64_t>(b) * a.num_heads);
+  int row, L, err;
+  const int npages = request_pages(a, b, row, L, err);
+  const int ns = (npages + a.pages_per_split - 1) / a.pages_per_split;
+  if (ns <= 1) return;  // written by the split kernel (or zero-filled there)
+
+  const int64_t base = (static_cast<int64_t>(b) * a.num_heads + hq) * a.max_splits;
+  const float* ml = a.ws_ml + base * 2;
+  const float4* accp = reinterpret_cast<const float4*>(a.ws_acc + base * kD) + lane;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  float l = 0.f;
+  for (int s = 0; s < ns; ++s) {
+    const float sc = b200::ex2(ml[2 * s] - M);
+    l += sc * ml[2 * s + 1];
+    const float4 v = accp[s * (kD / 4)];
+    o.x += sc * v.x;
+    o.y += sc * v.y;
+    o.z += sc * v.z;
+    o.w += sc * v.w;
+  }
+  const float inv = 1.f / l;
+  uint2 packed;
+  packed.x = b200::pack_bf16x2(o.x * inv, o.y * inv);
+  packed.y = b200::pack_bf16x2(o.z * inv, o.w * inv);
+  *reinterpret_cast<uint2*>(a.out + b * a.o_b + hq * a.o_h + lane * 4) = packed;
+}
+
+bool mult8(int64_t s) { return (s & 7) == 0; }
+
+int max_splits_for(int max_pages, int pps) { return (max_pages + pps - 1) / pps; }
+
+std::mutex g_attr_mu;
+bool g_attr_done[64] = {false};
+
+int ensure_smem_attr(int dev) {
+  if (dev < 0) return B200_ERR_CUDA;
+  if (dev < 64 && g_attr_done[dev]) return B200_OK;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (dev < 64 && g_attr_done[dev]) return B200_OK;
+  cudaError_t e = cudaFuncSetAttribute(paged_decode_split_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return B200_ERR_CUDA;
+  if (dev < 64) g_attr_done[dev] = true;
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_paged_decode_default_split(int batch, int num_kv_heads, int max_pages) {
+  (void)batch;
+  (void)num_kv_heads;
+  (void)max_pages;
+  return kDefaultPagesPerSplit;
+}
+
+extern "C" size_t b200_paged_decode_workspace_size(int batch, int num_heads, int max_pages,
+                                                   int pages_per_split) {
+  if (batch <= 0 || num_heads <= 0 || max_pages <= 0) return 0;
+  if (pages_per_split <= 0) pages_per_split = kDefaultPagesPerSplit;
+  const int ms = max_splits_for(max_pages, pages_per_split);
+  if (ms <= 1) return 0;
+  return static_cast<size_t>(batch) * num_heads * ms * (kD + 2) * sizeof(float);
+}
+
+extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                 const void* k_pool, const void* v_pool, int64_t kv_stride_blk,
+                                 int64_t kv_stride_h, int64_t kv_stride_slot,
+                                 const int32_t* block_table, int64_t bt_stride_row,
+                                 const int32_t* seq_lens, const int32_t* row_ids, void* out,
+                                 int64_t out_stride_b, int64_t out_stride_h, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                 int num_blocks, int max_pages, int max_requests, float scale,
+                                 int pages_per_split, void* workspace, size_t workspace_bytes,
+                                 int32_t* dev_status, void* stream) {
+  if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || max_pages <= 0 ||
+      max_requests <= 0 || bt_stride_row <= 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return B200_OK;
+  if (!q || !k_pool || !v_pool || !block_table || !seq_lens || !row_ids || !out)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != kD || block_size != kBS) return B200_ERR_UNSUPPORTED;
+  if (num_heads % num_kv_heads != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int G = num_heads / num_kv_heads;
+  if (G > kMaxG) return B200_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(batch) * num_kv_heads > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  if (pages_per_split <= 0) pages_per_split = kDefaultPagesPerSplit;
+  if (pages_per_split > kMaxPagesPerSplit) return B200_ERR_INVALID_ARGUMENT;
+  if (!b200host::aligned16(q) || !b200host::aligned16(out) || !b200host::aligned16(k_pool) ||
+      !b200host::aligned16(v_pool))
+    return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {q_stride_b, q_stride_h, out_stride_b, out_stride_h,
+                             kv_stride_blk, kv_stride_h, kv_stride_slot};
+  for (int64_t s : strides)
+    if (!mult8(s)) return B200_ERR_ALIGNMENT;
+
+  const int ms = max_splits_for(max_pages, pages_per_split);
+  if (ms > 65535) return B200_ERR_INVALID_ARGUMENT;
+  const size_t need =
+      b200_paged_decode_workspace_size(batch, num_heads, max_pages, pages_per_split);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !b200host::aligned16(workspace)))
+    return B200_ERR_WORKSPACE;
+
+  // TMA maps over one layer of the pool: (d=128, slot=16, kv head, block)
+  CUtensorMap kmap, vmap;
+  {
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kBS),
+                                static_cast<cuuint64_t>(num_kv_heads),
+                                static_cast<cuuint64_t>(num_blocks)};
+    const cuuint64_t strides_b[3] = {static_cast<cuuint64_t>(kv_stride_slot) * 2,
+                                     static_cast<cuuint64_t>(kv_stride_h) * 2,
+                                     static_cast<cuuint64_t>(kv_stride_blk) * 2};
+    const cuuint32_t box[4] = {64, kBS, 1, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (b200host::encode_tiled(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                               const_cast<void*>(k_pool), dims, strides_b, box, es,
+                               CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS ||
+        b200host::encode_tiled(&vmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                               const_cast<void*>(v_pool), dims, strides_b, box, es,
+                               CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS)
+      return B200_ERR_TENSOR_MAP;
+  }
+
+  DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_b = q_stride_b;
+  a.q_h = q_stride_h;
+  a.block_table = block_table;
+  a.bt_row = bt_stride_row;
+  a.seq_lens = seq_lens;
+  a.row_ids = row_ids;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_b = out_stride_b;
+  a.o_h = out_stride_h;
+  a.ws_acc = static_cast<float*>(workspace);
+  a.ws_ml = need > 0 ? a.ws_acc + static_cast<size_t>(batch) * num_heads * ms * kD : nullptr;
+  a.batch = batch;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = G;
+  a.num_blocks = num_blocks;
+  a.max_pages = max_pages;
+  a.max_requests = max_requests;
+  a.pages_per_split = pages_per_split;
+  a.max_splits = ms;
+  a.scale_log2 = scale * kLog2e;
+  a.dev_status = dev_status;
+
+  int st = ensure_smem_attr(b200host::current_device());
+  if (st != B200_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(ms));
+  paged_decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(kmap, vmap, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return B200_ERR_CUDA;
+  if (ms > 1) {
+    const int64_t warps = static_cast<int64_t>(batch) * num_heads;
+    const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+    paged_decode_merge_kernel<<<blocks, 256, 0, s>>>(a);
+    e = cudaGetLastError();
+  }
+  return b200host::status_from_cuda(e);
+}

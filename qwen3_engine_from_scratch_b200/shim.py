@@ -1,0 +1,71 @@
+"""Drop-in binding of the B200 kernels into the reference engine's modules.
+
+The reference imports its kernel entry points by name
+(qwen3/attention.py:26-28, qwen3/PagedKVcache.py:16) and selects them with
+environment switches read on every call:
+
+* decode:  ``QWEN3_PAGED_ATTN == "triton"`` (default; qwen3/attention.py:101-104,
+  144-147; qwen3/model.py:87-90) calls ``triton_paged_attention_decode[_batch]``;
+* prefill: ``QWEN3_FLASH_ATTN != "pytorch"`` (qwen3/attention.py:113-116,
+  162-165; qwen3/model.py:143-146) calls ``flash_attention_prefill_batched``;
+* the decode write goes through ``update_kv_batch_triton`` imported into
+  qwen3/PagedKVcache.py.
+
+``install()`` rebinds those module-level names to the B200 implementations, so
+the reference's own switches route to them and ``GraphRunner`` captures them
+unchanged.  Setting ``QWEN3_FLASH_ATTN=b200`` before importing this module
+installs it automatically.  ``QWEN3_PAGED_ATTN`` must stay ``triton`` (its
+default): the reference compares it with ``==`` and any other value silently
+routes decode to its PyTorch fallback.  ``uninstall()`` restores the originals.
+"""
+
+from __future__ import annotations
+
+import importlib
+import os
+
+from . import ops
+
+# (module, attribute) -> replacement
+_BINDINGS = {
+    ("qwen3.attention", "triton_paged_attention_decode"): ops.triton_paged_attention_decode,
+    ("qwen3.attention", "triton_paged_attention_decode_batch"): ops.triton_paged_attention_decode_batch,
+    ("qwen3.attention", "flash_attention_prefill_batched"): ops.flash_attention_prefill_batched,
+    ("qwen3.PagedKVcache", "update_kv_batch_triton"): ops.update_kv_batch_triton,
+    ("qwen3.kernels.paged_attention", "paged_attention_decode_triton"): ops.paged_attention_decode_triton,
+    ("qwen3.kernels.paged_attention", "triton_paged_attention_decode"): ops.triton_paged_attention_decode,
+    ("qwen3.kernels.paged_attention", "triton_paged_attention_decode_batch"): ops.triton_paged_attention_decode_batch,
+    ("qwen3.kernels.paged_attention", "update_kv_batch_triton"): ops.update_kv_batch_triton,
+    ("qwen3.kernels.flash_attention_varlen", "flash_attention_prefill"): ops.flash_attention_prefill,
+    ("qwen3.kernels.flash_attention_varlen", "flash_attention_prefill_batched"): ops.flash_attention_prefill_batched,
+}
+
+_saved: dict = {}
+
+
+def install() -> list[str]:
+    """Rebind the reference's kernel names to the B200 ops; returns what was bound."""
+    bound = []
+    for (mod_name, attr), fn in _BINDINGS.items():
+        mod = importlib.import_module(mod_name)
+        if (mod_name, attr) not in _saved:
+            _saved[(mod_name, attr)] = getattr(mod, attr)
+        setattr(mod, attr, fn)
+        bound.append(f"{mod_name}.{attr}")
+    if os.environ.get("QWEN3_PAGED_ATTN", "triton") != "triton":
+        raise RuntimeError("QWEN3_PAGED_ATTN must be 'triton' (the reference's gate) for the "
+                           "B200 decode kernel to be selected")
+    return bound
+
+
+def uninstall() -> None:
+    for (mod_name, attr), fn in list(_saved.items()):
+        setattr(importlib.import_module(mod_name), attr, fn)
+    _saved.clear()
+
+
+if os.environ.get("QWEN3_FLASH_ATTN") == "b200":
+    try:
+        install()
+    except ModuleNotFoundError:
+        pass  # the reference engine is not importable in this process
