@@ -238,6 +238,8 @@ def run_b200(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     w = workload(args.config, rank, world)
+    if args.layers > 0:
+        w["layers"] = args.layers
     st = build_decode_state(w, device, seed=1000 + rank)
     pool, caches, rows = st["pool"], st["caches"], st["rows"]
     q, k_new, v_new, B = st["q"], st["k_new"], st["v_new"], st["B"]
@@ -561,6 +563,8 @@ def main():
     ap.add_argument("--config", default="c2", choices=["c2", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="layers per step (default: 28 for c2); 1 gives a small case for profiling")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
