@@ -144,6 +144,34 @@ int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                       int32_t* dev_status, void* stream);
 
 /*
+ * Paged decode without a caller-provided workspace (allocation-free variant).
+ * No counterpart in the reference: its Triton decode needs no workspace, and
+ * the split-K design here does.  For callers that cannot allocate device
+ * memory when they launch decode -- engines that give nearly all HBM to the KV
+ * pool and run a fixed arena, FFI bindings holding raw device pointers but no
+ * device allocator, loops that must not pay cudaMalloc's latency or its
+ * implicit synchronisation.  Same arguments and results as b200_paged_decode
+ * minus the workspace: the split partials live in a file-scope device array of
+ * B200_DECODE_NOALLOC_SCRATCH_BYTES per GPU (held until process exit).
+ * Returns B200_ERR_WORKSPACE when b200_paged_decode_workspace_size(...) for
+ * these shapes exceeds that maximum.  Calls no allocator.  The first call on a
+ * device looks up the array's device address; make it before any stream
+ * capture on that device.  All calls on a device share the array: calls whose
+ * kernels overlap on the GPU (unordered streams) race and must not be issued.
+ */
+#define B200_DECODE_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int b200_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                              const void* k_pool, const void* v_pool,
+                              int64_t kv_stride_blk, int64_t kv_stride_h, int64_t kv_stride_slot,
+                              const int32_t* block_table, int64_t bt_stride_row,
+                              const int32_t* seq_lens, const int32_t* row_ids,
+                              void* out, int64_t out_stride_b, int64_t out_stride_h,
+                              int batch, int num_heads, int num_kv_heads, int head_dim,
+                              int block_size, int num_blocks, int max_pages, int max_requests,
+                              float scale, int pages_per_split,
+                              int32_t* dev_status, void* stream);
+
+/*
  * Varlen causal prefill attention.  Sequence i owns rows
  * [cu_seqlens[i], cu_seqlens[i] + len_i) of the packed q/k/v/out tensors, with
  * len_i = cu_seqlens[i+1] - cu_seqlens[i] when seq_lens_opt is NULL (packed

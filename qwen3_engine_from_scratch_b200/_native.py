@@ -60,6 +60,9 @@ SIGNATURES = {
                                _P, _I64, _P, _P, _P, _I64, _I64,
                                _I, _I, _I, _I, _I, _I, _I, _I, _F, _I,
                                _P, _SZ, _P, _P]),
+    "b200_paged_decode_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64,
+                                       _P, _I64, _P, _P, _P, _I64, _I64,
+                                       _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "b200_varlen_prefill": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                  _P, _I64, _I64, _P, _P, _I, _I, _I, _I, _I, _I,
                                  _F, _I, _P, _P]),
