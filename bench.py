@@ -71,6 +71,11 @@ def workload(config: str, rank: int, world: int):
         return dict(name="c4_paged_decode_qwen3_8b_sharded", H=32, Hkv=8, lens=lens, layers=1,
                     num_blocks=blocks, max_seq_len=32768, scaling="strong", batch_total=512,
                     all_lens=all_lens)
+    if config == "c3":
+        rng = np.random.default_rng(3000 + rank)
+        lens = rng.integers(64, 2048, size=32, endpoint=True)
+        return dict(name="c3_varlen_prefill_qwen3_0.6b", H=16, Hkv=8, lens=lens, layers=1,
+                    scaling="weak", batch_per_gpu=32)
     raise SystemExit(f"unknown config {config}")
 
 
@@ -81,6 +86,11 @@ def decode_bytes(lens, H, Hkv, D=HEAD_DIM, elem=2):
     qo = B * H * D * elem * 2
     tables = int(((lens + BLOCK - 1) // BLOCK).sum()) * 4
     return kv + qo + tables + B * 8
+
+
+def prefill_flops(lens, H, D=HEAD_DIM):
+    lens = np.asarray(lens, dtype=np.int64)
+    return int((4 * H * D * (lens * (lens + 1) // 2)).sum())
 
 
 def scatter_bytes(B, Hkv, D=HEAD_DIM, elem=2):
@@ -381,9 +391,89 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": args.steps * layers * launches_per_layer,
         "clocks": clocks.summary(),
     }
+    if not args.no_prefill:
+        try:
+            line["prefill"] = run_prefill(args, rank, world, local_rank, steps=10, warmup=3)
+        except RuntimeError as e:   # the prefill kernel is optional for the decode headline
+            line["prefill"] = {"error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_budget)
     return line
+
+
+def run_prefill(args, rank, world, local_rank, steps, warmup):
+    """Config 3: varlen causal prefill of 32 packed sequences (+ the slot scatter of
+    their K/V into a paged pool through a random slot_mapping), timed with CUDA events."""
+    import torch
+    import qwen3_engine_from_scratch_b200 as qb
+    from qwen3_engine_from_scratch_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    w = workload("c3", rank, world)
+    H, Hkv, D = w["H"], w["Hkv"], HEAD_DIM
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    T = int(lens.sum())
+    g = torch.Generator(device=device).manual_seed(77 + rank)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=device)
+    pos = torch.from_numpy(np.concatenate([np.arange(L) for L in lens])).to(device).float()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+    ang = pos[:, None] * inv[None]
+    cos = torch.cat([ang, ang], -1).cos()[:, None]
+    sin = torch.cat([ang, ang], -1).sin()[:, None]
+
+    def rms_rope(x):
+        x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+        return x * cos + torch.cat([-x[..., D // 2:], x[..., :D // 2]], -1) * sin
+
+    q = rms_rope(torch.randn(T, H, D, generator=g, device=device)).to(torch.bfloat16)
+    k = rms_rope(torch.randn(T, Hkv, D, generator=g, device=device)).to(torch.bfloat16)
+    v = torch.randn(T, Hkv, D, generator=g, device=device).to(torch.bfloat16)
+    nb = (T + 15) // 16 + 64
+    kp = torch.zeros(nb, 1, Hkv, 16, D, dtype=torch.bfloat16, device=device)
+    vp = torch.zeros_like(kp)
+    slots = torch.randperm(nb * 16, generator=g, device=device)[:T].to(torch.int64)
+    max_len = int(lens.max())
+    scale = D ** -0.5
+    out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+
+    def prefill():
+        ops._prefill(q, k, v, out, cu, None, max_len, scale, H, Hkv, D, False)
+
+    for _ in range(warmup):
+        prefill()
+        ops.kv_scatter_slots(k, v, kp, vp, slots)
+    torch.cuda.synchronize()
+    qb.check_device_status(device)
+    stream = torch.cuda.current_stream()
+    pa = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    pb = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    sb = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        pa[i].record(stream)
+        prefill()
+        pb[i].record(stream)
+        ops.kv_scatter_slots(k, v, kp, vp, slots)
+        sb[i].record(stream)
+    torch.cuda.synchronize()
+    qb.check_device_status(device)
+    p_ms = sum(a.elapsed_time(b) for a, b in zip(pa, pb)) / steps
+    s_ms = sum(a.elapsed_time(b) for a, b in zip(pb, sb)) / steps
+    flops = prefill_flops(lens, H)
+    sbytes = T * Hkv * D * 2 * 2 * 2 + T * 8
+    peaks, src = read_peaks()
+    tflops = flops / (p_ms / 1e3) / 1e12
+    return {"workload": w["name"], "tokens": T, "sequences": len(lens),
+            "lengths": "U[64,2048]", "heads": f"{H}/{Hkv}",
+            "ms_per_prefill": round(p_ms, 4), "tflops": round(tflops, 1),
+            "flops_per_launch": flops,
+            "roofline": {"kernel": "varlen_prefill_kernel", "bound": "tensor",
+                         "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4),
+                         "peak_source": src, "traffic": read_traffic("varlen_prefill_kernel")},
+            "scatter": {"ms": round(s_ms, 4), "bytes": sbytes,
+                        "gbs": round(sbytes / (s_ms / 1e3) / 1e9, 1),
+                        "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "gpu_launches_per_step": 2}
 
 
 def read_peaks():
@@ -560,9 +650,10 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers per step (default: 28 for c2); 1 gives a small case for profiling")
     args = ap.parse_args()
@@ -584,7 +675,19 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_b200(args, rank, world, local_rank)
+        if args.config == "c3":
+            torch.cuda.set_device(local_rank)
+            r = run_prefill(args, rank, world, local_rank, steps=args.steps, warmup=args.warmup)
+            line = None
+            if rank == 0:
+                line = {"metric": "varlen_prefill_tflops", "value": r["tflops"], "unit": "TFLOP/s",
+                        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                        "ms_per_step": r["ms_per_prefill"], "higher_is_better": True,
+                        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                        "data": "synthetic", "config": {"workload": r["workload"]},
+                        "roofline": r["roofline"], "detail": r}
+        else:
+            line = run_b200(args, rank, world, local_rank)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

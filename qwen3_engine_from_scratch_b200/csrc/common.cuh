@@ -66,6 +66,35 @@ B200_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   return false;
 }
 
+B200_DEVICE uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for phase `parity` with a wall-clock limit; also gives up as soon as
+// another CTA has recorded a timeout in the device status word, so a broken
+// pipeline ends the whole grid within about one limit.  Returns false on
+// give-up.
+B200_DEVICE bool mbar_wait_abortable(uint32_t bar, uint32_t parity, const int32_t* dev_status,
+                                     uint64_t limit_ns) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (dev_status != nullptr &&
+          (*reinterpret_cast<const volatile int32_t*>(dev_status) & B200_DEV_TIMEOUT))
+        return false;
+      const uint64_t t = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > limit_ns) {
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 B200_DEVICE uint64_t l2_policy_evict_first() {
   uint64_t pol;
