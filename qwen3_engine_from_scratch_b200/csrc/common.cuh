@@ -167,6 +167,23 @@ B200_DEVICE float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA/ALU pipes (no special-function unit), for x <= 126:
+// x = j + f with j = round(x) obtained by adding 1.5 * 2^23 (the integer lands
+// in the low mantissa bits), 2^f for f in [-0.5, 0.5] from a degree-3
+// polynomial fitted here for minimum relative error (max 7.5e-5), and 2^j
+// applied by adding j to the exponent field.  Inputs below -125 (and -inf)
+// are clamped to -125 so the exponent field never underflows into the sign
+// bit; the result, about 2^-125, is negligible next to the row maximum's 2^0.
+B200_DEVICE float ex2_fma(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  const float p =
+      fmaf(fmaf(fmaf(0.0551716685f, f, 0.2426111400f), f, 0.6932609677f), f, 0.9999280572f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 B200_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

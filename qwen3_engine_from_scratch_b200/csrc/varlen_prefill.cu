@@ -55,6 +55,9 @@ constexpr int kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of every kExpFmaPeriod columns, the first 2*kExpFmaPairs use ex2_fma.
+constexpr int kExpFmaPeriod = 8;
+constexpr int kExpFmaPairs = 2;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct PrefillArgs {
@@ -375,8 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        const float p0 = b200::ex2(fmaf(x[c], a.scale_log2, -m_used));
-        const float p1 = b200::ex2(fmaf(x[c + 1], a.scale_log2, -m_used));
+        // a fixed share of the exponentials runs on the FMA pipe so the
+        // special-function unit is not the bottleneck of the tile
+        const bool fma_pair = (c & (kExpFmaPeriod - 1)) < kExpFmaPairs * 2;
+        const float y0 = fmaf(x[c], a.scale_log2, -m_used);
+        const float y1 = fmaf(x[c + 1], a.scale_log2, -m_used);
+        const float p0 = fma_pair ? b200::ex2_fma(y0) : b200::ex2(y0);
+        const float p1 = fma_pair ? b200::ex2_fma(y1) : b200::ex2(y1);
         rowsum += p0 + p1;
         pk[c / 2] = b200::pack_bf16x2(p0, p1);
       }

@@ -69,6 +69,6 @@ def kv_head_tp_all_gather(local_out: torch.Tensor, group=None) -> torch.Tensor:
     import torch.distributed as dist
     n = dist.get_world_size(group)
     B, Hl, D = local_out.shape
-    buf = torch.empty((n, B, Hl, D), dtype=local_out.dtype, device=local_out.device)
+    buf = torch.empty((n * B, Hl, D), dtype=local_out.dtype, device=local_out.device)
     dist.all_gather_into_tensor(buf, local_out.contiguous(), group=group)
-    return buf.permute(1, 0, 2, 3).reshape(B, n * Hl * D)
+    return buf.view(n, B, Hl, D).permute(1, 0, 2, 3).reshape(B, n * Hl * D)

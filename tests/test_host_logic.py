@@ -1,0 +1,140 @@
+"""Host-side logic that needs no GPU: request sharding, the KV-head TP exchange
+(world size 2 over gloo), the shim's name binding, and the FMA-pipe exp2 method
+the prefill kernel uses."""
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REFERENCE = os.environ.get("QWEN3_REFERENCE", "/root/reference")
+
+
+def test_lpt_partition_balances_and_covers():
+    from qwen3_engine_from_scratch_b200.dist import lpt_partition, shard_loads, decode_cost
+    rng = np.random.default_rng(0)
+    lens = np.exp(rng.uniform(np.log(256), np.log(32768), size=512)).astype(int)
+    for n in (1, 2, 4, 8):
+        shards = lpt_partition(decode_cost(lens), n)
+        flat = sorted(i for s in shards for i in s)
+        assert flat == list(range(512))
+        loads = shard_loads(decode_cost(lens), shards)
+        # LPT bound: max load <= mean + max item
+        assert max(loads) <= sum(loads) / n + max(lens)
+        assert max(loads) / (sum(loads) / n) < 1.02
+    assert lpt_partition([5, 5, 5], 2) == [[0, 2], [1]]
+
+
+def test_lpt_prefill_cost_is_quadratic():
+    from qwen3_engine_from_scratch_b200.dist import prefill_cost
+    assert prefill_cost([1, 2, 2048]) == [1, 3, 2048 * 2049 // 2]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from qwen3_engine_from_scratch_b200.dist import kv_head_tp_all_gather, lpt_partition
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, H, D = 3, 16, 128
+        full = torch.arange(B * H * D, dtype=torch.float32).reshape(B, H, D)
+        hl = H // world
+        local = full[:, rank * hl:(rank + 1) * hl]
+        gathered = kv_head_tp_all_gather(local)
+        ok_tp = torch.equal(gathered, full.reshape(B, H * D))
+        # request sharding: every rank derives the same partition, no exchange needed
+        lens = [300, 20, 4000, 128, 77, 1000]
+        mine = lpt_partition(lens, world)[rank]
+        t = torch.tensor([sum(lens[i] for i in mine)], dtype=torch.float64)
+        dist.all_reduce(t)
+        q.put((rank, ok_tp, float(t.item())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world2_tp_gather_and_sharding():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [q.get(timeout=10) for _ in procs]
+    assert all(ok for _, ok, _ in res)
+    assert all(total == sum([300, 20, 4000, 128, 77, 1000]) for _, _, total in res)
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REFERENCE, "qwen3")),
+                    reason="reference checkout not present")
+def test_shim_binds_into_reference_modules(monkeypatch):
+    monkeypatch.syspath_prepend(REFERENCE)
+    import importlib
+    from qwen3_engine_from_scratch_b200 import ops, shim
+    bound = shim.install()
+    try:
+        attn = importlib.import_module("qwen3.attention")
+        kvc = importlib.import_module("qwen3.PagedKVcache")
+        assert attn.triton_paged_attention_decode_batch is ops.triton_paged_attention_decode_batch
+        assert attn.triton_paged_attention_decode is ops.triton_paged_attention_decode
+        assert attn.flash_attention_prefill_batched is ops.flash_attention_prefill_batched
+        assert kvc.update_kv_batch_triton is ops.update_kv_batch_triton
+        assert len(bound) == 10
+    finally:
+        shim.uninstall()
+    attn = importlib.import_module("qwen3.attention")
+    assert attn.triton_paged_attention_decode_batch is not ops.triton_paged_attention_decode_batch
+
+
+def test_reference_signatures_match():
+    """The drop-in names take the reference's positional arguments."""
+    import inspect
+    from qwen3_engine_from_scratch_b200 import ops
+    expect = {
+        "paged_attention_decode_triton": ["q", "k_buffer", "v_buffer", "block_table_2d",
+                                          "seq_lens_full", "row_ids", "block_size"],
+        "triton_paged_attention_decode": ["q", "k_new", "v_new", "kv_cache", "layer_idx", "scaling"],
+        "triton_paged_attention_decode_batch": ["q", "k_new", "v_new", "kv_caches", "layer_idx",
+                                                "scaling", "row_ids"],
+        "update_kv_batch_triton": ["k_new", "v_new", "k_buffer", "v_buffer", "seq_lens",
+                                   "block_table_2d", "row_ids", "layer_idx"],
+        "flash_attention_prefill": ["q", "k", "v", "cu_seqlens", "scale", "num_heads",
+                                    "num_kv_heads", "head_dim"],
+        "flash_attention_prefill_batched": ["q", "k", "v", "lens", "scaling", "num_heads",
+                                            "num_kv_heads", "head_dim"],
+    }
+    for name, params in expect.items():
+        got = list(inspect.signature(getattr(ops, name)).parameters)
+        assert got[:len(params)] == params, (name, got)
+
+
+def test_fma_exp2_method():
+    """The exponent-split + degree-3 polynomial 2^x of the prefill kernel
+    (common.cuh ex2_fma), restated in float32 numpy: relative error below
+    1e-4 on the range the softmax uses, finite and tiny below it."""
+    x = np.concatenate([np.linspace(-200, 8, 400001), [-np.inf, -125.0, -126.0]]).astype(np.float32)
+    xc = np.maximum(x, np.float32(-125))
+    t = (xc + np.float32(12582912.0)).astype(np.float32)
+    j = (t - np.float32(12582912.0)).astype(np.float32)
+    f = (xc - j).astype(np.float32)
+    c = [np.float32(v) for v in (0.0551716685, 0.2426111400, 0.6932609677, 0.9999280572)]
+    p = (((c[0] * f + c[1]) * f + c[2]) * f + c[3]).astype(np.float32)
+    res = (p.view(np.int32) + (t.view(np.int32) << 23)).view(np.float32)
+    assert np.isfinite(res).all() and (res > 0).all()
+    ok = x >= -125
+    rel = np.abs(res[ok].astype(np.float64) / np.exp2(x[ok].astype(np.float64)) - 1)
+    assert rel.max() < 1e-4
+    assert res[~ok].max() < 1e-37
