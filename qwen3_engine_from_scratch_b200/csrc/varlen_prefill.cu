@@ -2,32 +2,39 @@
 // cores (tcgen05 + TMEM), fed by TMA.  Replaces flash_attention_varlen_kernel
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
-// One CTA computes a 128-query tile of one query head of one sequence:
-//   warp 4      TMA producer: Q tile once, then K/V tiles of 128 keys into a
-//               2-stage ring (two 64-column boxes per tile, 128-byte swizzle).
-//   warp 5      MMA issuer (one thread): S = Q.K^T into one of two TMEM score
-//               buffers (M=128, N=128, K=16 per instruction, 8 instructions),
-//               O += P.V into the TMEM output accumulator; every group ends
-//               with tcgen05.commit on an mbarrier.
+// One CTA computes a 128-query tile of one query head of one sequence; two
+// CTAs fit on an SM (96 KB shared memory, 256 TMEM columns each), so one
+// CTA's softmax overlaps the other's tensor-core work.
+//   warp 4      TMA producer: lane 0 loads the Q tile once, then K tiles of
+//               64 keys into a 2-stage ring, each stage refilled as soon as
+//               its S = Q.K^T is done; lane 1 streams the V tiles, each stage
+//               refilled after its P.V (two 64-column boxes per tile,
+//               128-byte swizzle).
+//   warp 5      MMA issuer (one thread): S = Q.K^T (M=128, N=64, K=16 per
+//               instruction, 8 instructions) into one of two TMEM score
+//               buffers, O += P.V (M=128, N=128, 4 instructions) with P read
+//               from TMEM; each group ends with tcgen05.commit on an mbarrier.
 //   warps 0-3   softmax: thread r owns query row r (TMEM lane r); it loads its
-//               128 scores with tcgen05.ld, applies the causal / length mask,
-//               updates the running max (base 2) and sum in fp32, writes P as
-//               bf16 into a 128-byte-swizzled shared-memory tile (the A
-//               operand of the P.V MMA), and rescales its O row in TMEM only
-//               when the running max grew by more than 2^8 (otherwise the
-//               stale max keeps every P <= 2^8, exact in fp32).
+//               64 scores with tcgen05.ld, applies the causal / length mask,
+//               updates the running max (base 2) and sum in fp32 with tree
+//               reductions, and writes P as packed bf16 pairs over the first
+//               32 columns of the same score buffer (tcgen05.st).  Its O row
+//               in TMEM is rescaled only when the running max grew by more
+//               than 2^8 (otherwise the stale max keeps every P <= 2^8).
 // KV tiles strictly above the diagonal are never loaded (the reference
 // computes every KV block of the sequence, flash_attention_varlen.py:74-77).
 //
 // Operand layouts (UMMA canonical forms):
-//   Q, K  (128 rows x 128 d)  K-major, 128B swizzle: two 16 KB blocks of
+//   Q (128 x 128 d), K (64 x 128 d)  K-major, 128B swizzle: two blocks of
 //         [row][64 d]; descriptor SBO = 1024 B (8 rows), start += 32 B per K
-//         step inside a block, += 16 KB between blocks.
-//   P     (128 rows x 128 keys) K-major, same form.
-//   V     (128 keys x 128 d)  MN-major (d contiguous), 128B swizzle: LBO =
-//         16 KB between the two 64-d blocks, SBO = 1024 B (8 keys), start +=
-//         2 KB (16 keys) per K step.
-//   TMEM  columns [0,128) S0, [128,256) S1, [256,384) O; lane = query row.
+//         step inside a block, += block size between blocks.
+//   P     A operand in TMEM: lane = query row, column c = keys 2c, 2c+1.
+//   V (64 keys x 128 d)  MN-major (d contiguous), 128B swizzle: LBO = 8 KB
+//         between the two 64-d blocks, SBO = 1024 B (8 keys), start += 2 KB
+//         (16 keys) per K step.
+//   TMEM  columns [0,64) S0/P0, [64,128) S1/P1, [128,256) O; lane = query row.
+// MMAs issued by the one MMA thread execute in order, so S(j+2) overwriting
+// buffer j&1 follows the P.V that read P(j) from it.
 // Every mbarrier wait is bounded; TMEM is always freed before the CTA exits.
 #include <math.h>
 
@@ -39,25 +46,26 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kBM = 128;
-constexpr int kBN = 128;
+constexpr int kBN = 64;
 constexpr int kStages = 2;
-constexpr int kTileBytes = kBM * kD * 2;  // 32 KB
-constexpr int kBlockBytes = kTileBytes / 2;  // 16 KB: one 64-column swizzled block
+constexpr int kQBytes = kBM * kD * 2;       // 32 KB
+constexpr int kQBlock = kQBytes / 2;        // 16 KB: [128 rows][64 d] swizzled block
+constexpr int kKVBytes = kBN * kD * 2;      // 16 KB per K (or V) tile
+constexpr int kKVBlock = kKVBytes / 2;      // 8 KB: [64 rows][64 d]
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;
-constexpr int kSmemTiles = kOffP + kTileBytes;  // 192 KB
+constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kOffV = kOffK + kStages * kKVBytes;
+constexpr int kSmemTiles = kOffV + kStages * kKVBytes;  // 96 KB
 constexpr int kSmemBytes = kSmemTiles + 1024;
 constexpr int kThreads = 192;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO = 256;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS0 = 0, kColO = 2 * kBN;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Of every kExpFmaPeriod columns, the first 2*kExpFmaPairs use ex2_fma.
 constexpr int kExpFmaPeriod = 8;
-constexpr int kExpFmaPairs = 2;
+constexpr int kExpFmaPairs = 1;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct PrefillArgs {
@@ -74,11 +82,11 @@ struct __align__(8) Barriers {
   uint64_t q_full;
   uint64_t k_full[kStages];
   uint64_t v_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t k_empty[kStages];  // K stage free: its S = Q.K^T finished
+  uint64_t v_empty[kStages];  // V stage free: its P.V finished
   uint64_t s_full[2];
-  uint64_t s_free[2];
   uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t pv_done[2];  // P(j).V(j) finished, for j & 1
   uint32_t tmem_base;
   int32_t error;
 };
@@ -92,15 +100,15 @@ B200_DEVICE uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M=128, N=128.
-constexpr uint32_t idesc_bf16(bool b_mn_major) {
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M=128, N=n.
+constexpr uint32_t idesc_bf16(uint32_t n, bool b_mn_major) {
   return (1u << 4)                     // D format f32
          | (1u << 7)                   // A format bf16
          | (1u << 10)                  // B format bf16
          | (0u << 15)                  // A K-major
          | ((b_mn_major ? 1u : 0u) << 16)
-         | ((static_cast<uint32_t>(kBN) >> 3) << 17)   // N >> 3
-         | ((static_cast<uint32_t>(kBM) >> 4) << 24);  // M >> 4
+         | ((n >> 3) << 17)                              // N >> 3
+         | ((static_cast<uint32_t>(kBM) >> 4) << 24);    // M >> 4
 }
 
 B200_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -110,6 +118,17 @@ B200_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A operand from TMEM (lane = row, each column two K elements), B from smem.
+B200_DEVICE void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -184,7 +203,7 @@ B200_DEVICE bool wait_or_flag(uint32_t bar, uint32_t parity, Barriers* B, int32_
   return false;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     varlen_prefill_kernel(const __grid_constant__ CUtensorMap tmq,
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const PrefillArgs a) {
@@ -226,30 +245,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = b200::smem_u32(smem);
-  const uint32_t sQ = sbase + kOffQ, sK = sbase + kOffK, sV = sbase + kOffV, sP = sbase + kOffP;
+  const uint32_t sQ = sbase + kOffQ, sK = sbase + kOffK, sV = sbase + kOffV;
 
   const uint32_t bar_q = b200::smem_u32(&B.q_full);
   auto bar_k = [&](int s) { return b200::smem_u32(&B.k_full[s]); };
   auto bar_v = [&](int s) { return b200::smem_u32(&B.v_full[s]); };
-  auto bar_e = [&](int s) { return b200::smem_u32(&B.kv_empty[s]); };
+  auto bar_ke = [&](int s) { return b200::smem_u32(&B.k_empty[s]); };
+  auto bar_ve = [&](int s) { return b200::smem_u32(&B.v_empty[s]); };
   auto bar_sf = [&](int s) { return b200::smem_u32(&B.s_full[s]); };
-  auto bar_sr = [&](int s) { return b200::smem_u32(&B.s_free[s]); };
   const uint32_t bar_p = b200::smem_u32(&B.p_full);
-  const uint32_t bar_o = b200::smem_u32(&B.pv_done);
+  // pv_done[j & 1] completes once per P(j).V(j); its waiters ask for P(j).V(j)
+  // with parity (j >> 1) & 1.  The previous same-parity product P(j-2).V(j-2)
+  // has always completed by then (s_full(j) commits after every earlier MMA)
+  // and P(j+2).V(j+2) cannot have been issued, so the parity is unambiguous.
+  auto bar_o = [&](int j) { return b200::smem_u32(&B.pv_done[j & 1]); };
 
   if (threadIdx.x == 0) {
     b200::mbar_init(bar_q, 1);
     for (int s = 0; s < kStages; ++s) {
       b200::mbar_init(bar_k(s), 1);
       b200::mbar_init(bar_v(s), 1);
-      b200::mbar_init(bar_e(s), 1);
+      b200::mbar_init(bar_ke(s), 1);
+      b200::mbar_init(bar_ve(s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      b200::mbar_init(bar_sf(s), 1);
-      b200::mbar_init(bar_sr(s), 128);
-    }
+    for (int s = 0; s < 2; ++s) b200::mbar_init(bar_sf(s), 1);
     b200::mbar_init(bar_p, 128);
-    b200::mbar_init(bar_o, 1);
+    b200::mbar_init(bar_o(0), 1);
+    b200::mbar_init(bar_o(1), 1);
     B.error = 0;
     b200::fence_mbar_init();
   }
@@ -266,68 +288,76 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = B.tmem_base;
 
   if (warp == kProducerWarp) {
+    // lane 0 streams Q then the K tiles, lane 1 the V tiles: a K stage is
+    // refilled as soon as its S = Q.K^T is done, without waiting for P.V
     if (lane == 0) {
       b200::prefetch_tensormap(&tmq);
       b200::prefetch_tensormap(&tmk);
-      b200::prefetch_tensormap(&tmv);
-      b200::mbar_arrive_expect_tx(bar_q, kTileBytes);
+      b200::mbar_arrive_expect_tx(bar_q, kQBytes);
       b200::tma_load_3d(sQ, &tmq, bar_q, 0, h, start + m0);
-      b200::tma_load_3d(sQ + kBlockBytes, &tmq, bar_q, 64, h, start + m0);
+      b200::tma_load_3d(sQ + kQBlock, &tmq, bar_q, 64, h, start + m0);
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
-        if (j >= kStages && !wait_or_flag(bar_e(s), ((j >> 1) - 1) & 1, &B, a.dev_status)) break;
-        const int row = start + j * kBN;
-        const uint32_t dk = sK + s * kTileBytes, dv = sV + s * kTileBytes;
-        b200::mbar_arrive_expect_tx(bar_k(s), kTileBytes);
-        b200::tma_load_3d(dk, &tmk, bar_k(s), 0, hk, row);
-        b200::tma_load_3d(dk + kBlockBytes, &tmk, bar_k(s), 64, hk, row);
-        b200::mbar_arrive_expect_tx(bar_v(s), kTileBytes);
-        b200::tma_load_3d(dv, &tmv, bar_v(s), 0, hk, row);
-        b200::tma_load_3d(dv + kBlockBytes, &tmv, bar_v(s), 64, hk, row);
+        if (j >= kStages && !wait_or_flag(bar_ke(s), ((j >> 1) - 1) & 1, &B, a.dev_status)) break;
+        const uint32_t dk = sK + s * kKVBytes;
+        b200::mbar_arrive_expect_tx(bar_k(s), kKVBytes);
+        b200::tma_load_3d(dk, &tmk, bar_k(s), 0, hk, start + j * kBN);
+        b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, hk, start + j * kBN);
+      }
+    } else if (lane == 1) {
+      b200::prefetch_tensormap(&tmv);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (j >= kStages && !wait_or_flag(bar_ve(s), ((j >> 1) - 1) & 1, &B, a.dev_status)) break;
+        const uint32_t dv = sV + s * kKVBytes;
+        b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
+        b200::tma_load_3d(dv, &tmv, bar_v(s), 0, hk, start + j * kBN);
+        b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, hk, start + j * kBN);
       }
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16(false);
-      constexpr uint32_t idO = idesc_bf16(true);
+      constexpr uint32_t idS = idesc_bf16(kBN, false);
+      constexpr uint32_t idO = idesc_bf16(kD, true);
       bool ok = wait_or_flag(bar_q, 0, &B, a.dev_status);
       tc_fence_after();
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (j < n_kv) {
-          // ---- S(j) = Q . K_j^T into score buffer j & 1
+          // ---- S(j) = Q . K_j^T into score buffer j & 1.  The buffer last
+          // held P(j-2), read by the P.V issued before this point.
           const int s = j & 1;
           ok = wait_or_flag(bar_k(s), (j >> 1) & 1, &B, a.dev_status);
-          if (ok && j >= 2) ok = wait_or_flag(bar_sr(s), ((j >> 1) - 1) & 1, &B, a.dev_status);
           if (!ok) break;
           tc_fence_after();
           const uint32_t dS = tmem + kColS0 + s * kBN;
-          const uint32_t kt = sK + s * kTileBytes;
+          const uint32_t kt = sK + s * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kBlockBytes + (kk & 3) * 32;
-            umma_bf16(dS, smem_desc(sQ + off, 16, 1024), smem_desc(kt + off, 16, 1024), idS,
+            const uint32_t inblk = (kk & 3) * 32;
+            umma_bf16(dS, smem_desc(sQ + (kk >> 2) * kQBlock + inblk, 16, 1024),
+                      smem_desc(kt + (kk >> 2) * kKVBlock + inblk, 16, 1024), idS,
                       kk > 0 ? 1u : 0u);
           }
           umma_commit(bar_sf(s));
+          umma_commit(bar_ke(s));
         }
         if (j >= 1) {
-          // ---- O += P(j-1) . V_{j-1}
+          // ---- O += P(j-1) . V_{j-1}, P from TMEM
           const int jp = j - 1;
           const int s = jp & 1;
           ok = wait_or_flag(bar_p, jp & 1, &B, a.dev_status);
           if (ok) ok = wait_or_flag(bar_v(s), (jp >> 1) & 1, &B, a.dev_status);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t vt = sV + s * kTileBytes;
+          const uint32_t vt = sV + s * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint32_t pa = sP + (kk >> 2) * kBlockBytes + (kk & 3) * 32;
-            umma_bf16(tmem + kColO, smem_desc(pa, 16, 1024),
-                      smem_desc(vt + kk * 16 * 128, kBlockBytes, 1024), idO,
-                      (jp > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ts(tmem + kColO, tmem + kColS0 + s * kBN + kk * 8,
+                         smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
+                         (jp > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(bar_o);
-          umma_commit(bar_e(s));
+          umma_commit(bar_o(jp));
+          umma_commit(bar_ve(s));
         }
       }
     }
@@ -343,16 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(s), (j >> 1) & 1, &B, a.dev_status));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t sbuf = tmem + lane_addr + kColS0 + s * kBN;
       uint32_t xs[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tmem + lane_addr + kColS0 + s * kBN + c * 32, xs + c * 32);
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(sbuf + c * 32, xs + c * 32);
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld(xs + c * 32);
       float x[kBN];
 #pragma unroll
       for (int c = 0; c < kBN; ++c) x[c] = __uint_as_float(xs[c]);
-      tc_fence_before();
-      mbar_arrive(bar_sr(s));
 
       const int n0 = j * kBN;
       if (n0 + kBN - 1 > qpos || n0 + kBN > len) {
@@ -361,10 +390,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBN; ++c)
           if (c >= lim) x[c] = -INFINITY;
       }
-      float mx = x[0];
+      // tree max (8 independent chains)
+      float mq[8];
 #pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, x[c]);
-      mx *= a.scale_log2;
+      for (int i = 0; i < 8; ++i) mq[i] = x[i];
+#pragma unroll
+      for (int c = 8; c < kBN; ++c) mq[c & 7] = fmaxf(mq[c & 7], x[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                             fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))) *
+                       a.scale_log2;
       float alpha = 1.f;
       bool rescale = false;
       if (j == 0) {
@@ -374,57 +408,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = mx;
         rescale = true;
       }
-      float rowsum = 0.f;
+      float sq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[kBN / 2];
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        // a fixed share of the exponentials runs on the FMA pipe so the
-        // special-function unit is not the bottleneck of the tile
+        // a fixed share of the exponentials may run on the FMA pipe
         const bool fma_pair = (c & (kExpFmaPeriod - 1)) < kExpFmaPairs * 2;
         const float y0 = fmaf(x[c], a.scale_log2, -m_used);
         const float y1 = fmaf(x[c + 1], a.scale_log2, -m_used);
         const float p0 = fma_pair ? b200::ex2_fma(y0) : b200::ex2(y0);
         const float p1 = fma_pair ? b200::ex2_fma(y1) : b200::ex2(y1);
-        rowsum += p0 + p1;
+        sq[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = b200::pack_bf16x2(p0, p1);
       }
+      const float rowsum = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
 
-      if (j >= 1) {
-        // P buffer free and O updated by PV(j-1)
-        ok = __all_sync(0xffffffffu, wait_or_flag(bar_o, (j - 1) & 1, &B, a.dev_status));
+      // P(j) over the first half of its own score buffer (S(j) is consumed)
+      tmem_st32(sbuf, pk);
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O must hold P(j-1).V(j-1) before it is rescaled; tcgen05.ld/st are
+        // warp-collective, so the warp's rows rescale together (alpha == 1
+        // for rows whose max did not move)
+        ok = __all_sync(0xffffffffu,
+                        wait_or_flag(bar_o(j - 1), ((j - 1) >> 1) & 1, &B, a.dev_status));
         if (!ok) break;
         tc_fence_after();
-        // tcgen05.ld/st are warp-collective: rescale the warp's rows together
-        // (alpha == 1 for rows whose max did not move)
-        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t rr[32];
-            tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
-            tmem_wait_ld(rr);
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
+          tmem_wait_ld(rr);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-            tmem_st32(tmem + lane_addr + kColO + c * 32, rr);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+          tmem_st32(tmem + lane_addr + kColO + c * 32, rr);
         }
       }
       l = l * alpha + rowsum;
-      // P row r into the swizzled K-major tile: 16-byte chunk g of the row
-#pragma unroll
-      for (int g = 0; g < kBN / 8; ++g) {
-        const uint32_t addr = sP + (g >> 3) * kBlockBytes + r * 128 + (((g & 7) ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * g]),
-                     "r"(pk[4 * g + 1]), "r"(pk[4 * g + 2]), "r"(pk[4 * g + 3])
-                     : "memory");
-      }
-      b200::fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar_p);
     }
 
     // ---- epilogue: O / l -> bf16 rows
-    if (ok) ok = __all_sync(0xffffffffu, wait_or_flag(bar_o, (n_kv - 1) & 1, &B, a.dev_status));
+    if (ok)
+      ok = __all_sync(0xffffffffu, wait_or_flag(bar_o(n_kv - 1), ((n_kv - 1) >> 1) & 1, &B,
+                                                a.dev_status));
     tc_fence_after();
     if (ok) {
       const bool live = qpos < len;
@@ -432,21 +460,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = live ? 1.f / l : 0.f;
       __nv_bfloat16* orow =
           a.out + static_cast<int64_t>(start + qpos) * a.o_t + static_cast<int64_t>(h) * a.o_h;
+      uint32_t ov[kD];
 #pragma unroll
-      for (int c = 0; c < kD / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
-        tmem_wait_ld(rr);
-        if (live || pad) {
+      for (int c = 0; c < kD / 32; ++c) tmem_ld32(tmem + lane_addr + kColO + c * 32, ov + c * 32);
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = b200::pack_bf16x2(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv);
-            v.y = b200::pack_bf16x2(__uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
-            v.z = b200::pack_bf16x2(__uint_as_float(rr[i + 4]) * inv, __uint_as_float(rr[i + 5]) * inv);
-            v.w = b200::pack_bf16x2(__uint_as_float(rr[i + 6]) * inv, __uint_as_float(rr[i + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
-          }
+      for (int c = 0; c < kD / 32; ++c) tmem_wait_ld(ov + c * 32);
+      if (live || pad) {
+#pragma unroll
+        for (int i = 0; i < kD; i += 8) {
+          uint4 v;
+          v.x = b200::pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
+          v.y = b200::pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
+          v.z = b200::pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
+          v.w = b200::pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + i) = v;
         }
       }
     }
@@ -480,12 +507,12 @@ int ensure_smem_attr(int dev) {
 bool mult8(int64_t s) { return (s & 7) == 0; }
 
 int encode_rows_map(CUtensorMap* map, const void* base, int heads, int tokens, int64_t stride_t,
-                    int64_t stride_h) {
+                    int64_t stride_h, int box_rows) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(heads),
                               static_cast<cuuint64_t>(tokens)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_h) * 2,
                                  static_cast<cuuint64_t>(stride_t) * 2};
-  const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kBM)};
+  const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t es[3] = {1, 1, 1};
   return b200host::encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
                                 dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -520,9 +547,11 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
     if (!mult8(s)) return B200_ERR_ALIGNMENT;
 
   CUtensorMap tq, tk, tv;
-  int st = encode_rows_map(&tq, q, num_heads, total_tokens, q_stride_t, q_stride_h);
-  if (st == B200_OK) st = encode_rows_map(&tk, k, num_kv_heads, total_tokens, k_stride_t, k_stride_h);
-  if (st == B200_OK) st = encode_rows_map(&tv, v, num_kv_heads, total_tokens, v_stride_t, v_stride_h);
+  int st = encode_rows_map(&tq, q, num_heads, total_tokens, q_stride_t, q_stride_h, kBM);
+  if (st == B200_OK)
+    st = encode_rows_map(&tk, k, num_kv_heads, total_tokens, k_stride_t, k_stride_h, kBN);
+  if (st == B200_OK)
+    st = encode_rows_map(&tv, v, num_kv_heads, total_tokens, v_stride_t, v_stride_h, kBN);
   if (st != B200_OK) return st;
 
   PrefillArgs a;
