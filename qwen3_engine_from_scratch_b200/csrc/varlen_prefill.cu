@@ -2,9 +2,11 @@
 // cores (tcgen05 + TMEM), fed by TMA.  Replaces flash_attention_varlen_kernel
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
-// One CTA computes a 128-query tile of one query head of one sequence; two
-// CTAs fit on an SM (96 KB shared memory, 256 TMEM columns each), so one
-// CTA's softmax overlaps the other's tensor-core work.
+// Persistent: two CTAs per SM (96 KB shared memory, 256 TMEM columns each),
+// each looping over work items -- a 128-query tile of one query head of one
+// sequence -- taken heaviest first (the last tile of every sequence first);
+// one CTA's softmax overlaps the other's tensor-core work, and an item's Q
+// load and epilogue overlap its neighbours' pipeline.
 //   warp 4      TMA producer: lane 0 loads the Q tile once, then K tiles of
 //               64 keys into a 2-stage ring, each stage refilled as soon as
 //               its S = Q.K^T is done; lane 1 streams the V tiles, each stage
@@ -38,6 +40,8 @@
 // Every mbarrier wait is bounded; TMEM is always freed before the CTA exits.
 #include <math.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -63,9 +67,10 @@ constexpr int kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS0 = 0, kColO = 2 * kBN;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-// Of every kExpFmaPeriod columns, the first 2*kExpFmaPairs use ex2_fma.
+// Of every kExpFmaPeriod columns, the first 2 * FMA_PAIRS (kernel template
+// parameter) use ex2_fma; the rest use the special-function unit.
 constexpr int kExpFmaPeriod = 8;
-constexpr int kExpFmaPairs = 1;
+constexpr int kDefaultExpFmaPairs = 0;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct PrefillArgs {
@@ -74,19 +79,55 @@ struct PrefillArgs {
   __nv_bfloat16* out;
   int64_t o_t, o_h;
   int num_seqs, num_heads, group, max_seqlen, zero_pad;
+  int n_tiles;  // ceil(max_seqlen / 128)
+  int n_items;  // n_tiles * num_seqs * num_heads
   float scale_log2;
   int32_t* dev_status;
 };
 
+// One work item: a 128-query tile of one head of one sequence.  Items are
+// enumerated heaviest first (last tile of every sequence first), and a CTA
+// takes items blockIdx.x, blockIdx.x + gridDim.x, ...
+struct Item {
+  int start, len, m0, h, hk, n_kv;
+  bool compute;  // the tile has rows inside the sequence
+  bool zero;     // padded adapter: rows past the sequence are zero-filled
+};
+
+B200_DEVICE Item decode_item(const PrefillArgs& a, int i) {
+  Item it;
+  const int per_t = a.num_seqs * a.num_heads;
+  const int q = i / per_t;
+  const int rem = i - q * per_t;
+  const int seq = rem / a.num_heads;
+  it.h = rem - seq * a.num_heads;
+  it.hk = it.h / a.group;
+  it.m0 = (a.n_tiles - 1 - q) * kBM;
+  it.start = a.cu[seq];
+  it.len = a.lens != nullptr ? a.lens[seq] : a.cu[seq + 1] - it.start;
+  const bool valid = it.len >= 0 && it.len <= a.max_seqlen;
+  it.compute = valid && it.m0 < it.len;
+  it.zero = valid && !it.compute && a.zero_pad;
+  it.n_kv = it.compute ? (min(it.len, it.m0 + kBM) + kBN - 1) / kBN : 0;  // causal: keys < m0+128
+  if (!valid && q == a.n_tiles - 1 && it.h == 0 && threadIdx.x == 0)
+    b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
+  return it;
+}
+
+// Every barrier below completes once per use of its slot.  A waiter asks for
+// the n-th completion with parity (n >> 1) & 1 of slot n & 1 (or parity n & 1
+// for single-slot barriers); the pipeline order guarantees that slot has not
+// run two completions ahead of any waiter, so parities are unambiguous.
 struct __align__(8) Barriers {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;   // Q tile loaded / all S of its item issued and done
   uint64_t k_full[kStages];
   uint64_t v_full[kStages];
   uint64_t k_empty[kStages];  // K stage free: its S = Q.K^T finished
   uint64_t v_empty[kStages];  // V stage free: its P.V finished
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t pv_done[2];  // P(j).V(j) finished, for j & 1
+  uint64_t s_full[2];         // S(g) in TMEM buffer g & 1
+  uint64_t p_full[2];         // P(g) written over S(g)
+  uint64_t pv_done[2];        // P(g).V(g) finished
+  uint64_t o_free;            // the item's O was read by the softmax warps
   uint32_t tmem_base;
   int32_t error;
 };
@@ -203,6 +244,7 @@ B200_DEVICE bool wait_or_flag(uint32_t bar, uint32_t parity, Barriers* B, int32_
   return false;
 }
 
+template <int FMA_PAIRS>
 __global__ void __launch_bounds__(kThreads, 2)
     varlen_prefill_kernel(const __grid_constant__ CUtensorMap tmq,
                           const __grid_constant__ CUtensorMap tmk,
@@ -210,37 +252,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   __shared__ Barriers B;
 
-  const int tile = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) tiles first
-  const int h = blockIdx.y;
-  const int seq = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
   if (a.dev_status != nullptr &&
       (*reinterpret_cast<const volatile int32_t*>(a.dev_status) & B200_DEV_TIMEOUT))
     return;  // a pipeline already gave up: do not start new work until the host clears it
-  const int start = a.cu[seq];
-  const int len = a.lens != nullptr ? a.lens[seq] : a.cu[seq + 1] - start;
-  const int m0 = tile * kBM;
-  if (len < 0 || len > a.max_seqlen) {
-    if (threadIdx.x == 0 && tile == 0 && h == 0) b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
-    return;
-  }
-  if (m0 >= len) {
-    // tile entirely past the sequence: only the padded adapter wants zeros here
-    if (a.zero_pad) {
-      const int rows = min(kBM, a.max_seqlen - m0);
-      for (int i = threadIdx.x; i < rows * (kD / 8); i += kThreads) {
-        const int r = i / (kD / 8), c = i % (kD / 8);
-        *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(start + m0 + r) * a.o_t +
-                                  static_cast<int64_t>(h) * a.o_h + c * 8) = make_uint4(0, 0, 0, 0);
-      }
-    }
-    return;
-  }
-  const int hk = h / a.group;
-  const int kv_end = min(len, m0 + kBM);        // causal: keys < m0 + 128
-  const int n_kv = (kv_end + kBN - 1) / kBN;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -248,30 +264,31 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t sQ = sbase + kOffQ, sK = sbase + kOffK, sV = sbase + kOffV;
 
   const uint32_t bar_q = b200::smem_u32(&B.q_full);
+  const uint32_t bar_qe = b200::smem_u32(&B.q_empty);
   auto bar_k = [&](int s) { return b200::smem_u32(&B.k_full[s]); };
   auto bar_v = [&](int s) { return b200::smem_u32(&B.v_full[s]); };
   auto bar_ke = [&](int s) { return b200::smem_u32(&B.k_empty[s]); };
   auto bar_ve = [&](int s) { return b200::smem_u32(&B.v_empty[s]); };
-  auto bar_sf = [&](int s) { return b200::smem_u32(&B.s_full[s]); };
-  const uint32_t bar_p = b200::smem_u32(&B.p_full);
-  // pv_done[j & 1] completes once per P(j).V(j); its waiters ask for P(j).V(j)
-  // with parity (j >> 1) & 1.  The previous same-parity product P(j-2).V(j-2)
-  // has always completed by then (s_full(j) commits after every earlier MMA)
-  // and P(j+2).V(j+2) cannot have been issued, so the parity is unambiguous.
-  auto bar_o = [&](int j) { return b200::smem_u32(&B.pv_done[j & 1]); };
+  auto bar_sf = [&](int g) { return b200::smem_u32(&B.s_full[g & 1]); };
+  auto bar_p = [&](int g) { return b200::smem_u32(&B.p_full[g & 1]); };
+  auto bar_o = [&](int g) { return b200::smem_u32(&B.pv_done[g & 1]); };
+  const uint32_t bar_of = b200::smem_u32(&B.o_free);
 
   if (threadIdx.x == 0) {
     b200::mbar_init(bar_q, 1);
+    b200::mbar_init(bar_qe, 1);
     for (int s = 0; s < kStages; ++s) {
       b200::mbar_init(bar_k(s), 1);
       b200::mbar_init(bar_v(s), 1);
       b200::mbar_init(bar_ke(s), 1);
       b200::mbar_init(bar_ve(s), 1);
     }
-    for (int s = 0; s < 2; ++s) b200::mbar_init(bar_sf(s), 1);
-    b200::mbar_init(bar_p, 128);
-    b200::mbar_init(bar_o(0), 1);
-    b200::mbar_init(bar_o(1), 1);
+    for (int s = 0; s < 2; ++s) {
+      b200::mbar_init(bar_sf(s), 1);
+      b200::mbar_init(bar_p(s), 128);
+      b200::mbar_init(bar_o(s), 1);
+    }
+    b200::mbar_init(bar_of, 128);
     B.error = 0;
     b200::fence_mbar_init();
   }
@@ -288,194 +305,239 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = B.tmem_base;
 
   if (warp == kProducerWarp) {
-    // lane 0 streams Q then the K tiles, lane 1 the V tiles: a K stage is
+    // lane 0 streams Q and the K tiles, lane 1 the V tiles: a K stage is
     // refilled as soon as its S = Q.K^T is done, without waiting for P.V
     if (lane == 0) {
       b200::prefetch_tensormap(&tmq);
       b200::prefetch_tensormap(&tmk);
-      b200::mbar_arrive_expect_tx(bar_q, kQBytes);
-      b200::tma_load_3d(sQ, &tmq, bar_q, 0, h, start + m0);
-      b200::tma_load_3d(sQ + kQBlock, &tmq, bar_q, 64, h, start + m0);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (j >= kStages && !wait_or_flag(bar_ke(s), ((j >> 1) - 1) & 1, &B, a.dev_status)) break;
-        const uint32_t dk = sK + s * kKVBytes;
-        b200::mbar_arrive_expect_tx(bar_k(s), kKVBytes);
-        b200::tma_load_3d(dk, &tmk, bar_k(s), 0, hk, start + j * kBN);
-        b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, hk, start + j * kBN);
+      int n_item = 0, kc = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
+        const Item it = decode_item(a, i);
+        if (!it.compute) continue;
+        if (n_item > 0 && !(ok = wait_or_flag(bar_qe, (n_item - 1) & 1, &B, a.dev_status))) break;
+        b200::mbar_arrive_expect_tx(bar_q, kQBytes);
+        b200::tma_load_3d(sQ, &tmq, bar_q, 0, it.h, it.start + it.m0);
+        b200::tma_load_3d(sQ + kQBlock, &tmq, bar_q, 64, it.h, it.start + it.m0);
+        for (int j = 0; j < it.n_kv; ++j, ++kc) {
+          const int s = kc & 1;
+          if (kc >= kStages && !(ok = wait_or_flag(bar_ke(s), ((kc >> 1) - 1) & 1, &B, a.dev_status)))
+            break;
+          const uint32_t dk = sK + s * kKVBytes;
+          b200::mbar_arrive_expect_tx(bar_k(s), kKVBytes);
+          b200::tma_load_3d(dk, &tmk, bar_k(s), 0, it.hk, it.start + j * kBN);
+          b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, it.hk, it.start + j * kBN);
+        }
+        ++n_item;
       }
     } else if (lane == 1) {
       b200::prefetch_tensormap(&tmv);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (j >= kStages && !wait_or_flag(bar_ve(s), ((j >> 1) - 1) & 1, &B, a.dev_status)) break;
-        const uint32_t dv = sV + s * kKVBytes;
-        b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
-        b200::tma_load_3d(dv, &tmv, bar_v(s), 0, hk, start + j * kBN);
-        b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, hk, start + j * kBN);
+      int vc = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
+        const Item it = decode_item(a, i);
+        for (int j = 0; j < it.n_kv; ++j, ++vc) {
+          const int s = vc & 1;
+          if (vc >= kStages && !(ok = wait_or_flag(bar_ve(s), ((vc >> 1) - 1) & 1, &B, a.dev_status)))
+            break;
+          const uint32_t dv = sV + s * kKVBytes;
+          b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
+          b200::tma_load_3d(dv, &tmv, bar_v(s), 0, it.hk, it.start + j * kBN);
+          b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, it.hk, it.start + j * kBN);
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(kBN, false);
       constexpr uint32_t idO = idesc_bf16(kD, true);
-      bool ok = wait_or_flag(bar_q, 0, &B, a.dev_status);
-      tc_fence_after();
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          // ---- S(j) = Q . K_j^T into score buffer j & 1.  The buffer last
-          // held P(j-2), read by the P.V issued before this point.
-          const int s = j & 1;
-          ok = wait_or_flag(bar_k(s), (j >> 1) & 1, &B, a.dev_status);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t dS = tmem + kColS0 + s * kBN;
-          const uint32_t kt = sK + s * kKVBytes;
+      int n_item = 0, g0 = 0;  // g = global index of S / P / P.V products in this CTA
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
+        const Item it = decode_item(a, i);
+        if (!it.compute) continue;
+        if (!(ok = wait_or_flag(bar_q, n_item & 1, &B, a.dev_status))) break;
+        tc_fence_after();
+        for (int j = 0; j <= it.n_kv; ++j) {
+          if (j < it.n_kv) {
+            // ---- S(g) = Q . K^T into buffer g & 1 (it last held P(g-2), whose
+            // P.V was issued before this point; MMAs execute in issue order)
+            const int g = g0 + j;
+            const int s = g & 1;
+            if (!(ok = wait_or_flag(bar_k(s), (g >> 1) & 1, &B, a.dev_status))) break;
+            tc_fence_after();
+            const uint32_t dS = tmem + kColS0 + s * kBN;
+            const uint32_t kt = sK + s * kKVBytes;
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t inblk = (kk & 3) * 32;
-            umma_bf16(dS, smem_desc(sQ + (kk >> 2) * kQBlock + inblk, 16, 1024),
-                      smem_desc(kt + (kk >> 2) * kKVBlock + inblk, 16, 1024), idS,
-                      kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kD / 16; ++kk) {
+              const uint32_t inblk = (kk & 3) * 32;
+              umma_bf16(dS, smem_desc(sQ + (kk >> 2) * kQBlock + inblk, 16, 1024),
+                        smem_desc(kt + (kk >> 2) * kKVBlock + inblk, 16, 1024), idS,
+                        kk > 0 ? 1u : 0u);
+            }
+            umma_commit(bar_sf(g));
+            umma_commit(bar_ke(s));
+            if (j == it.n_kv - 1) umma_commit(bar_qe);
           }
-          umma_commit(bar_sf(s));
-          umma_commit(bar_ke(s));
-        }
-        if (j >= 1) {
-          // ---- O += P(j-1) . V_{j-1}, P from TMEM
-          const int jp = j - 1;
-          const int s = jp & 1;
-          ok = wait_or_flag(bar_p, jp & 1, &B, a.dev_status);
-          if (ok) ok = wait_or_flag(bar_v(s), (jp >> 1) & 1, &B, a.dev_status);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t vt = sV + s * kKVBytes;
+          if (j >= 1) {
+            // ---- O += P(g) . V(g), P from TMEM
+            const int g = g0 + j - 1;
+            const int s = g & 1;
+            if (!(ok = wait_or_flag(bar_p(g), (g >> 1) & 1, &B, a.dev_status))) break;
+            if (!(ok = wait_or_flag(bar_v(s), (g >> 1) & 1, &B, a.dev_status))) break;
+            if (j == 1 && n_item > 0 &&
+                !(ok = wait_or_flag(bar_of, (n_item - 1) & 1, &B, a.dev_status)))
+              break;
+            tc_fence_after();
+            const uint32_t vt = sV + s * kKVBytes;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            umma_bf16_ts(tmem + kColO, tmem + kColS0 + s * kBN + kk * 8,
-                         smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
-                         (jp > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              umma_bf16_ts(tmem + kColO, tmem + kColS0 + s * kBN + kk * 8,
+                           smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
+                           (j > 1 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bar_o(g));
+            umma_commit(bar_ve(s));
           }
-          umma_commit(bar_o(jp));
-          umma_commit(bar_ve(s));
         }
+        g0 += it.n_kv;
+        ++n_item;
       }
     }
   } else {
     // ---------------------------------------------------------- softmax
     const int r = threadIdx.x;  // query row in the tile == TMEM lane
-    const int qpos = m0 + r;     // position within the sequence
     const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
+    int g0 = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int s = j & 1;
-      ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(s), (j >> 1) & 1, &B, a.dev_status));
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t sbuf = tmem + lane_addr + kColS0 + s * kBN;
-      uint32_t xs[kBN];
+    for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
+      const Item it = decode_item(a, i);
+      if (!it.compute) {
+        if (it.zero && it.m0 + r < a.max_seqlen) {
+          __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + it.m0 + r) * a.o_t +
+                                static_cast<int64_t>(it.h) * a.o_h;
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(sbuf + c * 32, xs + c * 32);
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld(xs + c * 32);
-      float x[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN; ++c) x[c] = __uint_as_float(xs[c]);
-
-      const int n0 = j * kBN;
-      if (n0 + kBN - 1 > qpos || n0 + kBN > len) {
-        const int lim = min(qpos + 1, len) - n0;  // keys [n0, n0 + lim) are visible
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (c >= lim) x[c] = -INFINITY;
+          for (int c = 0; c < kD; c += 8)
+            *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+        }
+        continue;
       }
-      // tree max (8 independent chains)
-      float mq[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mq[i] = x[i];
-#pragma unroll
-      for (int c = 8; c < kBN; ++c) mq[c & 7] = fmaxf(mq[c & 7], x[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
-                             fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))) *
-                       a.scale_log2;
-      float alpha = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_used = mx;
-      } else if (mx > m_used + kRescaleThreshold) {
-        alpha = b200::ex2(m_used - mx);
-        m_used = mx;
-        rescale = true;
-      }
-      float sq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        // a fixed share of the exponentials may run on the FMA pipe
-        const bool fma_pair = (c & (kExpFmaPeriod - 1)) < kExpFmaPairs * 2;
-        const float y0 = fmaf(x[c], a.scale_log2, -m_used);
-        const float y1 = fmaf(x[c + 1], a.scale_log2, -m_used);
-        const float p0 = fma_pair ? b200::ex2_fma(y0) : b200::ex2(y0);
-        const float p1 = fma_pair ? b200::ex2_fma(y1) : b200::ex2(y1);
-        sq[(c >> 1) & 7] += p0 + p1;
-        pk[c / 2] = b200::pack_bf16x2(p0, p1);
-      }
-      const float rowsum = ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
-
-      // P(j) over the first half of its own score buffer (S(j) is consumed)
-      tmem_st32(sbuf, pk);
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O must hold P(j-1).V(j-1) before it is rescaled; tcgen05.ld/st are
-        // warp-collective, so the warp's rows rescale together (alpha == 1
-        // for rows whose max did not move)
-        ok = __all_sync(0xffffffffu,
-                        wait_or_flag(bar_o(j - 1), ((j - 1) >> 1) & 1, &B, a.dev_status));
+      const int qpos = it.m0 + r;  // position within the sequence
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j) {
+        const int g = g0 + j;
+        const int s = g & 1;
+        ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(g), (g >> 1) & 1, &B, a.dev_status));
         if (!ok) break;
         tc_fence_after();
+        const uint32_t sbuf = tmem + lane_addr + kColS0 + s * kBN;
+        uint32_t xs[kBN];
 #pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t rr[32];
-          tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
-          tmem_wait_ld(rr);
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(sbuf + c * 32, xs + c * 32);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-          tmem_st32(tmem + lane_addr + kColO + c * 32, rr);
-        }
-      }
-      l = l * alpha + rowsum;
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar_p);
-    }
+        for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld(xs + c * 32);
+        float x[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) x[c] = __uint_as_float(xs[c]);
 
-    // ---- epilogue: O / l -> bf16 rows
-    if (ok)
-      ok = __all_sync(0xffffffffu, wait_or_flag(bar_o(n_kv - 1), ((n_kv - 1) >> 1) & 1, &B,
-                                                a.dev_status));
-    tc_fence_after();
-    if (ok) {
-      const bool live = qpos < len;
-      const bool pad = !live && a.zero_pad && qpos < a.max_seqlen;
-      const float inv = live ? 1.f / l : 0.f;
-      __nv_bfloat16* orow =
-          a.out + static_cast<int64_t>(start + qpos) * a.o_t + static_cast<int64_t>(h) * a.o_h;
+        const int n0 = j * kBN;
+        if (n0 + kBN - 1 > qpos || n0 + kBN > it.len) {
+          const int lim = min(qpos + 1, it.len) - n0;  // keys [n0, n0 + lim) are visible
+#pragma unroll
+          for (int c = 0; c < kBN; ++c)
+            if (c >= lim) x[c] = -INFINITY;
+        }
+        // tree max (8 independent chains)
+        float mq[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mq[e] = x[e];
+#pragma unroll
+        for (int c = 8; c < kBN; ++c) mq[c & 7] = fmaxf(mq[c & 7], x[c]);
+        const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                               fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))) *
+                         a.scale_log2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m_used = mx;
+        } else if (mx > m_used + kRescaleThreshold) {
+          alpha = b200::ex2(m_used - mx);
+          m_used = mx;
+          rescale = true;
+        }
+        float sq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[kBN / 2];
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          // a fixed share of the exponentials runs on the FMA pipe
+          const bool fma_pair = (c & (kExpFmaPeriod - 1)) < FMA_PAIRS * 2;
+          const float y0 = fmaf(x[c], a.scale_log2, -m_used);
+          const float y1 = fmaf(x[c + 1], a.scale_log2, -m_used);
+          const float p0 = fma_pair ? b200::ex2_fma(y0) : b200::ex2(y0);
+          const float p1 = fma_pair ? b200::ex2_fma(y1) : b200::ex2(y1);
+          sq[(c >> 1) & 7] += p0 + p1;
+          pk[c / 2] = b200::pack_bf16x2(p0, p1);
+        }
+        const float rowsum =
+            ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
+
+        // P(g) over the first half of its own score buffer (S(g) is consumed)
+        tmem_st32(sbuf, pk);
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O must hold everything up to P(g-1).V(g-1) before it is rescaled;
+          // tcgen05.ld/st are warp-collective, so the warp's rows rescale
+          // together (alpha == 1 for rows whose max did not move)
+          ok = __all_sync(0xffffffffu, wait_or_flag(bar_o(g - 1), ((g - 1) >> 1) & 1, &B,
+                                                    a.dev_status));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < kD / 32; ++c) {
+            uint32_t rr[32];
+            tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
+            tmem_wait_ld(rr);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+            tmem_st32(tmem + lane_addr + kColO + c * 32, rr);
+          }
+        }
+        l = l * alpha + rowsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p(g));
+      }
+      if (!ok) break;
+
+      // ---- epilogue: O / l -> bf16 rows; O is released before the stores
+      const int glast = g0 + it.n_kv - 1;
+      ok = __all_sync(0xffffffffu,
+                      wait_or_flag(bar_o(glast), (glast >> 1) & 1, &B, a.dev_status));
+      if (!ok) break;
+      tc_fence_after();
       uint32_t ov[kD];
 #pragma unroll
       for (int c = 0; c < kD / 32; ++c) tmem_ld32(tmem + lane_addr + kColO + c * 32, ov + c * 32);
 #pragma unroll
       for (int c = 0; c < kD / 32; ++c) tmem_wait_ld(ov + c * 32);
+      tc_fence_before();
+      mbar_arrive(bar_of);
+      const bool live = qpos < it.len;
+      const bool pad = !live && a.zero_pad && qpos < a.max_seqlen;
       if (live || pad) {
+        const float inv = live ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
+                              static_cast<int64_t>(it.h) * a.o_h;
 #pragma unroll
-        for (int i = 0; i < kD; i += 8) {
+        for (int e = 0; e < kD; e += 8) {
           uint4 v;
-          v.x = b200::pack_bf16x2(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv);
-          v.y = b200::pack_bf16x2(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv);
-          v.z = b200::pack_bf16x2(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv);
-          v.w = b200::pack_bf16x2(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + i) = v;
+          v.x = b200::pack_bf16x2(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv);
+          v.y = b200::pack_bf16x2(__uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
+          v.z = b200::pack_bf16x2(__uint_as_float(ov[e + 4]) * inv, __uint_as_float(ov[e + 5]) * inv);
+          v.w = b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv, __uint_as_float(ov[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + e) = v;
         }
       }
+      g0 += it.n_kv;
     }
   }
 
@@ -492,16 +554,35 @@ __global__ void __launch_bounds__(kThreads, 2)
 std::mutex g_attr_mu;
 bool g_attr_done[64] = {false};
 
+template <int P>
+cudaError_t set_smem_attr() {
+  return cudaFuncSetAttribute(varlen_prefill_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBytes);
+}
+
 int ensure_smem_attr(int dev) {
   if (dev < 0) return B200_ERR_CUDA;
   if (dev < 64 && g_attr_done[dev]) return B200_OK;
   std::lock_guard<std::mutex> lk(g_attr_mu);
   if (dev < 64 && g_attr_done[dev]) return B200_OK;
-  if (cudaFuncSetAttribute(varlen_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSmemBytes) != cudaSuccess)
+  if (set_smem_attr<0>() != cudaSuccess || set_smem_attr<1>() != cudaSuccess ||
+      set_smem_attr<2>() != cudaSuccess || set_smem_attr<3>() != cudaSuccess ||
+      set_smem_attr<4>() != cudaSuccess)
     return B200_ERR_CUDA;
   if (dev < 64) g_attr_done[dev] = true;
   return B200_OK;
+}
+
+// Share of the softmax exponentials evaluated on the FMA pipe, in pairs of
+// every 8 columns (0..4); B200_PREFILL_EXP_FMA_PAIRS overrides the default
+// for tuning.
+int exp_fma_pairs() {
+  static const int v = [] {
+    const char* e = getenv("B200_PREFILL_EXP_FMA_PAIRS");
+    if (e == nullptr || *e < '0' || *e > '4' || e[1] != 0) return kDefaultExpFmaPairs;
+    return *e - '0';
+  }();
+  return v;
 }
 
 bool mult8(int64_t s) { return (s & 7) == 0; }
@@ -537,7 +618,6 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
   if (!q || !k || !v || !out || !cu_seqlens) return B200_ERR_INVALID_ARGUMENT;
   if (head_dim != kD) return B200_ERR_UNSUPPORTED;
   if (num_heads % num_kv_heads != 0) return B200_ERR_INVALID_ARGUMENT;
-  if (num_heads > 65535 || num_seqs > 65535) return B200_ERR_INVALID_ARGUMENT;
   if (!b200host::aligned16(q) || !b200host::aligned16(k) || !b200host::aligned16(v) ||
       !b200host::aligned16(out))
     return B200_ERR_ALIGNMENT;
@@ -565,14 +645,26 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
   a.group = num_heads / num_kv_heads;
   a.max_seqlen = max_seqlen;
   a.zero_pad = zero_pad_rows != 0;
+  a.n_tiles = (max_seqlen + kBM - 1) / kBM;
+  const int64_t n_items = static_cast<int64_t>(a.n_tiles) * num_seqs * num_heads;
+  if (n_items > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  a.n_items = static_cast<int>(n_items);
   a.scale_log2 = scale * kLog2e;
   a.dev_status = dev_status;
 
   st = ensure_smem_attr(b200host::current_device());
   if (st != B200_OK) return st;
-  dim3 grid(static_cast<unsigned>((max_seqlen + kBM - 1) / kBM), static_cast<unsigned>(num_heads),
-            static_cast<unsigned>(num_seqs));
-  varlen_prefill_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk,
-                                                                                            tv, a);
+  const int sms = b200host::sm_count(b200host::current_device());
+  if (sms <= 0) return B200_ERR_CUDA;
+  const int64_t ctas = n_items < int64_t(2) * sms ? n_items : int64_t(2) * sms;  // 2 per SM
+  dim3 grid(static_cast<unsigned>(ctas));
+  cudaStream_t st_ = static_cast<cudaStream_t>(stream);
+  switch (exp_fma_pairs()) {
+    case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+    case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+    case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+    case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+    default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+  }
   return b200host::status_from_cuda(cudaGetLastError());
 }
