@@ -52,6 +52,10 @@ typedef enum {
 /* Human-readable text for a b200_status value. */
 const char* b200_status_string(int status);
 
+/* Text of the last CUDA error an entry point of this library met on the
+ * calling thread (behind a B200_ERR_CUDA return). */
+const char* b200_last_cuda_error_string(void);
+
 /* ABI version of this library (major*100 + minor). */
 int b200_abi_version(void);
 
@@ -180,11 +184,16 @@ int b200_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_strid
  * kv head h / (num_heads/num_kv_heads); fp32 online softmax, bf16 output.
  * Replaces flash_attention_varlen_kernel / flash_attention_prefill
  * (qwen3/kernels/flash_attention_varlen.py:25-194) without its host sync:
- * `max_seqlen` (>= every len_i) sizes the grid.  With zero_pad_rows != 0 the
- * rows [cu_seqlens[i] + len_i, cu_seqlens[i] + max_seqlen) of `out` are set to
- * zero, as the padded-batch adapter does (flash_attention_varlen.py:255-257).
+ * `max_seqlen` (>= every len_i, <= 262144) sizes the work list.  With
+ * zero_pad_rows != 0 the rows [cu_seqlens[i] + len_i, cu_seqlens[i] +
+ * max_seqlen) of `out` are set to zero, as the padded-batch adapter does
+ * (flash_attention_varlen.py:255-257).
  * q (T, H, D), k/v (T, Hkv, D): token and head strides in elements, head_dim
  * stride 1; out (T, H, D) with strides (token, head).  head_dim must be 128.
+ * work_counter (nullable): two int32 in device memory, zero at launch; the
+ * kernel hands out work items through them (balanced dynamically) and leaves
+ * them zero when it finishes.  Launches that may overlap on the GPU need
+ * separate counters.  NULL selects a fixed, slightly less balanced order.
  */
 int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         const void* k, int64_t k_stride_t, int64_t k_stride_h,
@@ -193,7 +202,8 @@ int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         const int32_t* cu_seqlens, const int32_t* seq_lens_opt,
                         int num_seqs, int total_tokens, int max_seqlen,
                         int num_heads, int num_kv_heads, int head_dim,
-                        float scale, int zero_pad_rows, int32_t* dev_status, void* stream);
+                        float scale, int zero_pad_rows, int32_t* work_counter,
+                        int32_t* dev_status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,7 @@ _SZ = ctypes.c_size_t
 SIGNATURES = {
     "b200_status_string": (ctypes.c_char_p, [_I]),
     "b200_abi_version": (_I, []),
+    "b200_last_cuda_error_string": (ctypes.c_char_p, []),
     "b200_device_sm_count": (_I, []),
     "b200_kv_scatter_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                   _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
@@ -65,7 +66,7 @@ SIGNATURES = {
                                        _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "b200_varlen_prefill": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                  _P, _I64, _I64, _P, _P, _I, _I, _I, _I, _I, _I,
-                                 _F, _I, _P, _P]),
+                                 _F, _I, _P, _P, _P]),
 }
 
 _lib = None
@@ -104,7 +105,10 @@ def status_string(code: int) -> str:
 def check(code: int, what: str) -> None:
     """Map a non-zero C status to RuntimeError (the reference raises on bad input too)."""
     if code != B200_OK:
-        raise RuntimeError(f"{what} failed: {status_string(code)} (status {code})")
+        detail = ""
+        if code == B200_ERR_CUDA:
+            detail = f": {load().b200_last_cuda_error_string().decode()}"
+        raise RuntimeError(f"{what} failed: {status_string(code)}{detail} (status {code})")
 
 
 def describe_dev_status(bits: int) -> str:

@@ -50,7 +50,17 @@ int sm_count(int device) {
   return n;
 }
 
-int status_from_cuda(cudaError_t e) { return e == cudaSuccess ? B200_OK : B200_ERR_CUDA; }
+namespace {
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+}
+
+int status_from_cuda(cudaError_t e) {
+  if (e == cudaSuccess) return B200_OK;
+  g_last_cuda_error = e;
+  return B200_ERR_CUDA;
+}
+
+cudaError_t last_cuda_error() { return g_last_cuda_error; }
 
 }  // namespace b200host
 
@@ -70,6 +80,11 @@ const char* b200_status_string(int status) {
 }
 
 int b200_abi_version(void) { return 100; }
+
+const char* b200_last_cuda_error_string(void) {
+  const cudaError_t e = b200host::last_cuda_error();
+  return e == cudaSuccess ? "no CUDA error recorded" : cudaGetErrorString(e);
+}
 
 int b200_device_sm_count(void) { return b200host::sm_count(b200host::current_device()); }
 

@@ -184,6 +184,13 @@ B200_DEVICE float ex2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// max of three floats in one instruction (sm_100 three-input max.f32)
+B200_DEVICE float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 B200_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -206,7 +213,8 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
 
 int current_device();
 int sm_count(int device);
-int status_from_cuda(cudaError_t e);
+int status_from_cuda(cudaError_t e);  // records e for b200_last_cuda_error_string
+cudaError_t last_cuda_error();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -2,11 +2,14 @@
 // cores (tcgen05 + TMEM), fed by TMA.  Replaces flash_attention_varlen_kernel
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
-// Persistent: two CTAs per SM (96 KB shared memory, 256 TMEM columns each),
-// each looping over work items -- a 128-query tile of one query head of one
-// sequence -- taken heaviest first (the last tile of every sequence first);
-// one CTA's softmax overlaps the other's tensor-core work, and an item's Q
-// load and epilogue overlap its neighbours' pipeline.
+// Persistent: two CTAs per SM (about 110 KB shared memory, 256 TMEM columns
+// each) loop over work items -- a 128-query tile of one query head of one
+// sequence.  Every CTA builds the same work list in shared memory: only the
+// non-empty tiles, heaviest first (tile index descending, sequences sorted by
+// length), and takes items from a global counter (dynamic balance) or, without
+// one, in a fixed boustrophedon order.  One CTA's softmax overlaps the other's
+// tensor-core work, and an item's Q load and epilogue overlap its neighbours'
+// pipeline.
 //   warp 4      TMA producer: lane 0 loads the Q tile once, then K tiles of
 //               64 keys into a 2-stage ring, each stage refilled as soon as
 //               its S = Q.K^T is done; lane 1 streams the V tiles, each stage
@@ -72,45 +75,59 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kExpFmaPeriod = 8;
 constexpr int kDefaultExpFmaPairs = 0;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxSeqs = 256;               // sequences per launch (the host splits larger batches)
+constexpr int kMaxTiles = 2048;             // 128-query tiles per sequence (max_seqlen <= 262144)
+constexpr int kRing = 4;                    // item-index ring between the scheduler and the roles
+constexpr int kRingConsumers = 2 + 128;     // V lane, MMA thread, softmax threads
 
 struct PrefillArgs {
   const int32_t* cu;
   const int32_t* lens;  // nullable
   __nv_bfloat16* out;
   int64_t o_t, o_h;
-  int num_seqs, num_heads, group, max_seqlen, zero_pad;
-  int n_tiles;  // ceil(max_seqlen / 128)
-  int n_items;  // n_tiles * num_seqs * num_heads
+  int num_seqs, num_heads, group, max_seqlen, zero_pad, total_tokens;
+  int n_tiles;          // ceil(max_seqlen / 128)
   float scale_log2;
   int32_t* dev_status;
+  int32_t* sched;       // nullable: [0] next item, [1] CTAs done (zero at launch, reset at exit)
 };
 
-// One work item: a 128-query tile of one head of one sequence.  Items are
-// enumerated heaviest first (last tile of every sequence first), and a CTA
-// takes items blockIdx.x, blockIdx.x + gridDim.x, ...
+// Work list shared by every CTA (each CTA builds the same one in shared
+// memory): the non-empty (tile, sequence, head) items, heaviest first -- tile
+// index descending (tile m attends to about 2m+2 K/V tiles of 64 keys),
+// sequences in descending order of their tile count, so the sequences that
+// reach tile m are a prefix of the sorted order.
+struct WorkList {
+  int len[kMaxSeqs];
+  int start[kMaxSeqs];
+  uint32_t key[kMaxSeqs];        // sorted: (kMaxTiles - 1 - tiles) << 16 | sequence
+  int prefix[kMaxTiles + 1];     // items before step u (tile n_tiles - 1 - u)
+  int pad_prefix[kMaxSeqs + 1];  // padded adapter: zero rows before sequence s (all heads)
+  unsigned char pad_ok[kMaxSeqs];  // rows [len, max_seqlen) of sequence s lie inside the output
+  int n_items;
+  int ring[kRing];
+};
+
 struct Item {
   int start, len, m0, h, hk, n_kv;
-  bool compute;  // the tile has rows inside the sequence
-  bool zero;     // padded adapter: rows past the sequence are zero-filled
 };
 
-B200_DEVICE Item decode_item(const PrefillArgs& a, int i) {
+B200_DEVICE Item decode_item(const PrefillArgs& a, const WorkList& W, int k) {
+  int lo = 0, hi = a.n_tiles;  // step u: largest with prefix[u] <= k
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (W.prefix[mid] <= k) lo = mid; else hi = mid;
+  }
+  const int rem = k - W.prefix[lo];
+  const int rank = rem / a.num_heads;
   Item it;
-  const int per_t = a.num_seqs * a.num_heads;
-  const int q = i / per_t;
-  const int rem = i - q * per_t;
-  const int seq = rem / a.num_heads;
-  it.h = rem - seq * a.num_heads;
+  it.h = rem - rank * a.num_heads;
   it.hk = it.h / a.group;
-  it.m0 = (a.n_tiles - 1 - q) * kBM;
-  it.start = a.cu[seq];
-  it.len = a.lens != nullptr ? a.lens[seq] : a.cu[seq + 1] - it.start;
-  const bool valid = it.len >= 0 && it.len <= a.max_seqlen;
-  it.compute = valid && it.m0 < it.len;
-  it.zero = valid && !it.compute && a.zero_pad;
-  it.n_kv = it.compute ? (min(it.len, it.m0 + kBM) + kBN - 1) / kBN : 0;  // causal: keys < m0+128
-  if (!valid && q == a.n_tiles - 1 && it.h == 0 && threadIdx.x == 0)
-    b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
+  const int seq = static_cast<int>(W.key[rank] & 0xFFFFu);
+  it.start = W.start[seq];
+  it.len = W.len[seq];
+  it.m0 = (a.n_tiles - 1 - lo) * kBM;
+  it.n_kv = (min(it.len, it.m0 + kBM) + kBN - 1) / kBN;  // causal: keys < m0 + 128
   return it;
 }
 
@@ -128,6 +145,7 @@ struct __align__(8) Barriers {
   uint64_t p_full[2];         // P(g) written over S(g)
   uint64_t pv_done[2];        // P(g).V(g) finished
   uint64_t o_free;            // the item's O was read by the softmax warps
+  uint64_t ring_full[kRing], ring_empty[kRing];
   uint32_t tmem_base;
   int32_t error;
 };
@@ -244,6 +262,70 @@ B200_DEVICE bool wait_or_flag(uint32_t bar, uint32_t parity, Barriers* B, int32_
   return false;
 }
 
+// Build the work list (every CTA computes the same one).  All threads call.
+B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
+  const int n = a.num_seqs;
+  int p2 = 1;
+  while (p2 < n) p2 <<= 1;
+  for (int s = threadIdx.x; s < p2; s += kThreads) {
+    if (s < n) {
+      const int start = a.cu[s];
+      int len = a.lens != nullptr ? a.lens[s] : a.cu[s + 1] - start;
+      const int rows = a.zero_pad ? a.max_seqlen : len;  // rows this sequence writes
+      const bool bad = len < 0 || len > a.max_seqlen || start < 0 ||
+                       static_cast<int64_t>(start) + rows > a.total_tokens;
+      if (bad) {
+        b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
+        len = 0;
+      }
+      W.start[s] = start;
+      W.len[s] = len;
+      W.pad_ok[s] = bad ? 0 : 1;
+      const int nt = (len + kBM - 1) / kBM;
+      W.key[s] = (static_cast<uint32_t>(kMaxTiles - 1 - nt) << 16) | static_cast<uint32_t>(s);
+    } else {
+      W.key[s] = 0xFFFFFFFFu;
+    }
+  }
+  __syncthreads();
+  // bitonic sort, ascending key = descending tile count, then sequence id
+  for (int k = 2; k <= p2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < p2; i += kThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t x = W.key[i], y = W.key[ixj];
+          if ((x > y) == ((i & k) == 0)) {
+            W.key[i] = y;
+            W.key[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) {
+    // prefix over steps u (tile m = n_tiles - 1 - u): sequences with more than
+    // m tiles are the first `cnt` of the sorted order
+    int cnt = 0, acc = 0;
+    for (int u = 0; u < a.n_tiles; ++u) {
+      const int m = a.n_tiles - 1 - u;
+      while (cnt < n && static_cast<int>(kMaxTiles - 1 - (W.key[cnt] >> 16)) > m) ++cnt;
+      W.prefix[u] = acc;
+      acc += cnt * a.num_heads;
+    }
+    W.prefix[a.n_tiles] = acc;
+    W.n_items = acc;
+    int pad = 0;
+    for (int s2 = 0; s2 < n; ++s2) {
+      W.pad_prefix[s2] = pad;
+      pad += a.zero_pad && W.pad_ok[s2] ? (a.max_seqlen - W.len[s2]) * a.num_heads : 0;
+    }
+    W.pad_prefix[n] = pad;
+  }
+  __syncthreads();
+}
+
 template <int FMA_PAIRS>
 __global__ void __launch_bounds__(kThreads, 2)
     varlen_prefill_kernel(const __grid_constant__ CUtensorMap tmq,
@@ -251,12 +333,17 @@ __global__ void __launch_bounds__(kThreads, 2)
                           const __grid_constant__ CUtensorMap tmv, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Barriers B;
+  __shared__ WorkList W;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (a.dev_status != nullptr &&
-      (*reinterpret_cast<const volatile int32_t*>(a.dev_status) & B200_DEV_TIMEOUT))
-    return;  // a pipeline already gave up: do not start new work until the host clears it
+  // a pipeline already gave up: start no new work until the host clears the status
+  const bool aborted =
+      a.dev_status != nullptr &&
+      (*reinterpret_cast<const volatile int32_t*>(a.dev_status) & B200_DEV_TIMEOUT);
+
+  if (!aborted) {
+  build_work_list(a, W);
 
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -273,6 +360,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto bar_p = [&](int g) { return b200::smem_u32(&B.p_full[g & 1]); };
   auto bar_o = [&](int g) { return b200::smem_u32(&B.pv_done[g & 1]); };
   const uint32_t bar_of = b200::smem_u32(&B.o_free);
+  auto bar_rf = [&](int n) { return b200::smem_u32(&B.ring_full[n & (kRing - 1)]); };
+  auto bar_re = [&](int n) { return b200::smem_u32(&B.ring_empty[n & (kRing - 1)]); };
 
   if (threadIdx.x == 0) {
     b200::mbar_init(bar_q, 1);
@@ -289,6 +378,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       b200::mbar_init(bar_o(s), 1);
     }
     b200::mbar_init(bar_of, 128);
+    for (int r = 0; r < kRing; ++r) {
+      b200::mbar_init(bar_rf(r), 1);
+      b200::mbar_init(bar_re(r), kRingConsumers);
+    }
     B.error = 0;
     b200::fence_mbar_init();
   }
@@ -304,18 +397,37 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
 
+  // the roles read the n-th item of this CTA from the ring (-1 ends the list)
+  auto next_item = [&](int n, bool& ok) -> int {
+    ok = wait_or_flag(bar_rf(n), (n / kRing) & 1, &B, a.dev_status);
+    const int k = ok ? W.ring[n & (kRing - 1)] : -1;
+    mbar_arrive(bar_re(n));
+    return k;
+  };
+
   if (warp == kProducerWarp) {
     // lane 0 streams Q and the K tiles, lane 1 the V tiles: a K stage is
     // refilled as soon as its S = Q.K^T is done, without waiting for P.V
     if (lane == 0) {
       b200::prefetch_tensormap(&tmq);
       b200::prefetch_tensormap(&tmk);
-      int n_item = 0, kc = 0;
+      int kc = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
-        const Item it = decode_item(a, i);
-        if (!it.compute) continue;
-        if (n_item > 0 && !(ok = wait_or_flag(bar_qe, (n_item - 1) & 1, &B, a.dev_status))) break;
+      for (int n = 0; ok; ++n) {
+        // scheduler: the next item from the global counter, or without one
+        // the fixed boustrophedon order over the CTAs
+        const int round = n / static_cast<int>(gridDim.x);
+        int k = a.sched != nullptr
+                    ? atomicAdd(&a.sched[0], 1)
+                    : round * gridDim.x + ((round & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+        if (k >= W.n_items) k = -1;
+        if (n >= kRing && !(ok = wait_or_flag(bar_re(n), ((n / kRing) - 1) & 1, &B, a.dev_status)))
+          break;
+        W.ring[n & (kRing - 1)] = k;
+        mbar_arrive(bar_rf(n));
+        if (k < 0) break;
+        const Item it = decode_item(a, W, k);
+        if (n > 0 && !(ok = wait_or_flag(bar_qe, (n - 1) & 1, &B, a.dev_status))) break;
         b200::mbar_arrive_expect_tx(bar_q, kQBytes);
         b200::tma_load_3d(sQ, &tmq, bar_q, 0, it.h, it.start + it.m0);
         b200::tma_load_3d(sQ + kQBlock, &tmq, bar_q, 64, it.h, it.start + it.m0);
@@ -328,14 +440,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           b200::tma_load_3d(dk, &tmk, bar_k(s), 0, it.hk, it.start + j * kBN);
           b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, it.hk, it.start + j * kBN);
         }
-        ++n_item;
       }
     } else if (lane == 1) {
       b200::prefetch_tensormap(&tmv);
       int vc = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
-        const Item it = decode_item(a, i);
+      for (int n = 0; ok; ++n) {
+        const int k = next_item(n, ok);
+        if (!ok || k < 0) break;
+        const Item it = decode_item(a, W, k);
         for (int j = 0; j < it.n_kv; ++j, ++vc) {
           const int s = vc & 1;
           if (vc >= kStages && !(ok = wait_or_flag(bar_ve(s), ((vc >> 1) - 1) & 1, &B, a.dev_status)))
@@ -351,11 +464,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(kBN, false);
       constexpr uint32_t idO = idesc_bf16(kD, true);
-      int n_item = 0, g0 = 0;  // g = global index of S / P / P.V products in this CTA
+      int g0 = 0;  // g = global index of S / P / P.V products in this CTA
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
-        const Item it = decode_item(a, i);
-        if (!it.compute) continue;
+      for (int n_item = 0; ok; ++n_item) {
+        const int k = next_item(n_item, ok);
+        if (!ok || k < 0) break;
+        const Item it = decode_item(a, W, k);
         if (!(ok = wait_or_flag(bar_q, n_item & 1, &B, a.dev_status))) break;
         tc_fence_after();
         for (int j = 0; j <= it.n_kv; ++j) {
@@ -401,27 +515,41 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
         g0 += it.n_kv;
-        ++n_item;
       }
     }
   } else {
     // ---------------------------------------------------------- softmax
     const int r = threadIdx.x;  // query row in the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+
+    // padded adapter: zero the rows past every sequence (spread over all CTAs)
+    if (a.zero_pad) {
+      const int total = W.pad_prefix[a.num_seqs];
+      for (int z = blockIdx.x * 128 + r; z < total; z += gridDim.x * 128) {
+        int lo = 0, hi = a.num_seqs;
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (W.pad_prefix[mid] <= z) lo = mid; else hi = mid;
+        }
+        const int rem = z - W.pad_prefix[lo];
+        const int pad_rows = a.max_seqlen - W.len[lo];
+        const int hh = rem / pad_rows;
+        const int row = W.len[lo] + (rem - hh * pad_rows);
+        __nv_bfloat16* orow = a.out + static_cast<int64_t>(W.start[lo] + row) * a.o_t +
+                              static_cast<int64_t>(hh) * a.o_h;
+#pragma unroll
+        for (int c = 0; c < kD; c += 8)
+          *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+
     int g0 = 0;
     bool ok = true;
-    for (int i = blockIdx.x; ok && i < a.n_items; i += gridDim.x) {
-      const Item it = decode_item(a, i);
-      if (!it.compute) {
-        if (it.zero && it.m0 + r < a.max_seqlen) {
-          __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + it.m0 + r) * a.o_t +
-                                static_cast<int64_t>(it.h) * a.o_h;
-#pragma unroll
-          for (int c = 0; c < kD; c += 8)
-            *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
-        }
-        continue;
-      }
+    for (int n = 0; ok; ++n) {
+      const int k = next_item(n, ok);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || k < 0) break;
+      const Item it = decode_item(a, W, k);
       const int qpos = it.m0 + r;  // position within the sequence
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j) {
@@ -521,10 +649,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int c = 0; c < kD / 32; ++c) tmem_wait_ld(ov + c * 32);
       tc_fence_before();
       mbar_arrive(bar_of);
-      const bool live = qpos < it.len;
-      const bool pad = !live && a.zero_pad && qpos < a.max_seqlen;
-      if (live || pad) {
-        const float inv = live ? 1.f / l : 0.f;
+      if (qpos < it.len) {  // rows past the sequence are zeroed by the pass above
+        const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
                               static_cast<int64_t>(it.h) * a.o_h;
 #pragma unroll
@@ -548,6 +674,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
+  }
+  }  // !aborted
+
+  // the last CTA to finish leaves the schedule counter zeroed for the next launch
+  if (a.sched != nullptr && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&a.sched[1], 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(&a.sched[0], 0);
+      atomicExch(&a.sched[1], 0);
+    }
   }
 }
 
@@ -611,13 +747,17 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
                                    const int32_t* cu_seqlens, const int32_t* seq_lens_opt,
                                    int num_seqs, int total_tokens, int max_seqlen, int num_heads,
                                    int num_kv_heads, int head_dim, float scale, int zero_pad_rows,
-                                   int32_t* dev_status, void* stream) {
+                                   int32_t* work_counter, int32_t* dev_status, void* stream) {
   if (num_seqs < 0 || total_tokens < 0 || max_seqlen < 0 || num_heads <= 0 || num_kv_heads <= 0)
     return B200_ERR_INVALID_ARGUMENT;
   if (num_seqs == 0 || total_tokens == 0 || max_seqlen == 0) return B200_OK;
   if (!q || !k || !v || !out || !cu_seqlens) return B200_ERR_INVALID_ARGUMENT;
   if (head_dim != kD) return B200_ERR_UNSUPPORTED;
   if (num_heads % num_kv_heads != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int n_tiles = (max_seqlen + kBM - 1) / kBM;
+  if (n_tiles > kMaxTiles) return B200_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(n_tiles) * kMaxSeqs * num_heads > 0x7fffffff)
+    return B200_ERR_INVALID_ARGUMENT;
   if (!b200host::aligned16(q) || !b200host::aligned16(k) || !b200host::aligned16(v) ||
       !b200host::aligned16(out))
     return B200_ERR_ALIGNMENT;
@@ -634,37 +774,41 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
     st = encode_rows_map(&tv, v, num_kv_heads, total_tokens, v_stride_t, v_stride_h, kBN);
   if (st != B200_OK) return st;
 
-  PrefillArgs a;
-  a.cu = cu_seqlens;
-  a.lens = seq_lens_opt;
-  a.out = static_cast<__nv_bfloat16*>(out);
-  a.o_t = o_stride_t;
-  a.o_h = o_stride_h;
-  a.num_seqs = num_seqs;
-  a.num_heads = num_heads;
-  a.group = num_heads / num_kv_heads;
-  a.max_seqlen = max_seqlen;
-  a.zero_pad = zero_pad_rows != 0;
-  a.n_tiles = (max_seqlen + kBM - 1) / kBM;
-  const int64_t n_items = static_cast<int64_t>(a.n_tiles) * num_seqs * num_heads;
-  if (n_items > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  a.n_items = static_cast<int>(n_items);
-  a.scale_log2 = scale * kLog2e;
-  a.dev_status = dev_status;
-
   st = ensure_smem_attr(b200host::current_device());
   if (st != B200_OK) return st;
   const int sms = b200host::sm_count(b200host::current_device());
   if (sms <= 0) return B200_ERR_CUDA;
-  const int64_t ctas = n_items < int64_t(2) * sms ? n_items : int64_t(2) * sms;  // 2 per SM
-  dim3 grid(static_cast<unsigned>(ctas));
-  cudaStream_t st_ = static_cast<cudaStream_t>(stream);
-  switch (exp_fma_pairs()) {
-    case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
-    case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
-    case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
-    case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
-    default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, st_>>>(tq, tk, tv, a); break;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int pairs = exp_fma_pairs();
+
+  // sequences are independent: launch at most kMaxSeqs of them at a time
+  for (int s0 = 0; s0 < num_seqs; s0 += kMaxSeqs) {
+    PrefillArgs a;
+    a.cu = cu_seqlens + s0;
+    a.lens = seq_lens_opt != nullptr ? seq_lens_opt + s0 : nullptr;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.o_t = o_stride_t;
+    a.o_h = o_stride_h;
+    a.num_seqs = num_seqs - s0 < kMaxSeqs ? num_seqs - s0 : kMaxSeqs;
+    a.num_heads = num_heads;
+    a.group = num_heads / num_kv_heads;
+    a.max_seqlen = max_seqlen;
+    a.zero_pad = zero_pad_rows != 0;
+    a.total_tokens = total_tokens;
+    a.n_tiles = n_tiles;
+    a.scale_log2 = scale * kLog2e;
+    a.dev_status = dev_status;
+    a.sched = work_counter;
+    dim3 grid(static_cast<unsigned>(2 * sms));  // two persistent CTAs per SM
+    switch (pairs) {
+      case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+    }
+    st = b200host::status_from_cuda(cudaGetLastError());
+    if (st != B200_OK) return st;
   }
-  return b200host::status_from_cuda(cudaGetLastError());
+  return B200_OK;
 }

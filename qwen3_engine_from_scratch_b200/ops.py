@@ -343,9 +343,34 @@ def triton_paged_attention_decode(q, k_new, v_new, kv_cache, layer_idx, scaling)
 # ---------------------------------------------------------------------------
 
 
+_counter_lock = threading.Lock()
+_counters: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _work_counter(device: torch.device) -> torch.Tensor:
+    """The prefill kernel's work counter for (device, current stream).
+
+    Two int32 that are zero at launch; the kernel hands out work items through
+    them and its last CTA zeroes them again, so launches on one stream (also
+    inside a captured graph) reuse the same pair.  Each stream gets its own
+    pair, because launches on different streams may overlap.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    t = _counters.get(key)
+    if t is None:
+        with _counter_lock:
+            t = _counters.get(key)
+            if t is None:
+                t = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
+                _counters[key] = t
+    return t
+
+
 def _prefill(q, k, v, out, cu_seqlens, seq_lens_opt, max_seqlen, scale, num_heads, num_kv_heads,
              head_dim, zero_pad_rows):
     lib = _native.load()
+    counter = _work_counter(q.device)
     st = lib.b200_varlen_prefill(
         q.data_ptr(), q.stride(0), q.stride(1),
         k.data_ptr(), k.stride(0), k.stride(1),
@@ -354,7 +379,7 @@ def _prefill(q, k, v, out, cu_seqlens, seq_lens_opt, max_seqlen, scale, num_head
         cu_seqlens.data_ptr(), seq_lens_opt.data_ptr() if seq_lens_opt is not None else None,
         cu_seqlens.numel() - 1 if seq_lens_opt is None else seq_lens_opt.numel(),
         q.shape[0], int(max_seqlen), num_heads, num_kv_heads, head_dim, float(scale),
-        int(zero_pad_rows), _status_ptr(q.device), _stream())
+        int(zero_pad_rows), counter.data_ptr(), _status_ptr(q.device), _stream())
     _native.check(st, "b200_varlen_prefill")
 
 

@@ -184,3 +184,45 @@ def test_prefill_argument_errors(cuda, native_lib):
     q16 = torch.zeros(8, 2, 128, dtype=torch.float16, device=cuda)
     with pytest.raises(AssertionError):
         qb.flash_attention_prefill(q16, q16, q16, cu, 0.1, 2, 2, 128)
+
+
+def test_work_counter_reset_fixed_order_and_graph_replay(cuda, native_lib):
+    """The dynamic schedule only decides which CTA computes an item, so the
+    result is bit-exact against the fixed order (no counter); the counter is
+    zero again after every launch, also across CUDA graph replays."""
+    import qwen3_engine_from_scratch_b200 as qb
+    from qwen3_engine_from_scratch_b200 import _native, ops
+    lens = [2048, 1, 700, 129, 1500, 64, 300, 1000] * 3
+    H, Hkv = 16, 8
+    q, k, v, cu = _rand_varlen(cuda, lens, H, Hkv, seed=21)
+    scale = 1 / math.sqrt(D)
+    out = qb.flash_attention_prefill(q, k, v, cu, scale, H, Hkv, D, max_seqlen=max(lens))
+    counter = ops._work_counter(q.device)
+    torch.cuda.synchronize()
+    assert counter.tolist() == [0, 0]
+    fixed = torch.empty_like(out)
+    lib = _native.load()
+    st = lib.b200_varlen_prefill(q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
+                                 k.stride(1), v.data_ptr(), v.stride(0), v.stride(1),
+                                 fixed.data_ptr(), fixed.stride(0), fixed.stride(1), cu.data_ptr(),
+                                 None, len(lens), q.shape[0], max(lens), H, Hkv, D, scale, 0, None,
+                                 ops._status_ptr(q.device), ops._stream())
+    _native.check(st, "b200_varlen_prefill")
+    torch.cuda.synchronize()
+    assert torch.equal(out, fixed)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        qb.flash_attention_prefill(q, k, v, cu, scale, H, Hkv, D, max_seqlen=max(lens))  # warm
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            o_g = qb.flash_attention_prefill(q, k, v, cu, scale, H, Hkv, D, max_seqlen=max(lens))
+            o_g2 = qb.flash_attention_prefill(q, k, v, cu, scale, H, Hkv, D, max_seqlen=max(lens))
+        for _ in range(3):
+            o_g.zero_()
+            g.replay()
+        s.synchronize()
+        assert ops._work_counter(q.device).tolist() == [0, 0]
+    torch.cuda.current_stream().wait_stream(s)
+    assert torch.equal(o_g, out) and torch.equal(o_g2, out)
