@@ -196,6 +196,47 @@ B200_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: one issue for two lanes)
+B200_DEVICE uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+B200_DEVICE void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+B200_DEVICE uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+B200_DEVICE uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ex2_fma on a pair with packed fp32 arithmetic: same method and result as
+// ex2_fma lane by lane (2^j applied as t_bits * 2^23 + p_bits, which equals the
+// shift-and-add of ex2_fma modulo 2^32).
+B200_DEVICE uint64_t ex2_fma2(uint64_t y) {
+  float a, b;
+  f2_unpack(y, a, b);
+  const uint64_t yc = f2_pack(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
+  const uint64_t t = f2_add(yc, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t j = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));
+  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), yc);
+  uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f,
+                      f2_pack(0.2426111400f, 0.2426111400f));
+  p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
+  p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
+  float t0, t1, p0, p1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, p0, p1);
+  return f2_pack(__int_as_float(__float_as_int(t0) * 8388608 + __float_as_int(p0)),
+                 __int_as_float(__float_as_int(t1) * 8388608 + __float_as_int(p1)));
+}
+
 B200_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 B200_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

@@ -2,44 +2,47 @@
 // cores (tcgen05 + TMEM), fed by TMA.  Replaces flash_attention_varlen_kernel
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
-// Persistent: two CTAs per SM (about 110 KB shared memory, 256 TMEM columns
-// each) loop over work items -- a 128-query tile of one query head of one
-// sequence.  Every CTA builds the same work list in shared memory: only the
-// non-empty tiles, heaviest first (tile index descending, sequences sorted by
-// length), and takes items from a global counter (dynamic balance) or, without
-// one, in a fixed boustrophedon order.  One CTA's softmax overlaps the other's
-// tensor-core work, and an item's Q load and epilogue overlap its neighbours'
-// pipeline.
-//   warp 4      TMA producer: lane 0 loads the Q tile once, then K tiles of
-//               64 keys into a 2-stage ring, each stage refilled as soon as
-//               its S = Q.K^T is done; lane 1 streams the V tiles, each stage
-//               refilled after its P.V (two 64-column boxes per tile,
-//               128-byte swizzle).
-//   warp 5      MMA issuer (one thread): S = Q.K^T (M=128, N=64, K=16 per
-//               instruction, 8 instructions) into one of two TMEM score
-//               buffers, O += P.V (M=128, N=128, 4 instructions) with P read
-//               from TMEM; each group ends with tcgen05.commit on an mbarrier.
-//   warps 0-3   softmax: thread r owns query row r (TMEM lane r); it loads its
-//               64 scores with tcgen05.ld, applies the causal / length mask,
-//               updates the running max (base 2) and sum in fp32 with tree
-//               reductions, and writes P as packed bf16 pairs over the first
-//               32 columns of the same score buffer (tcgen05.st).  Its O row
-//               in TMEM is rescaled only when the running max grew by more
-//               than 2^8 (otherwise the stale max keeps every P <= 2^8).
-// KV tiles strictly above the diagonal are never loaded (the reference
-// computes every KV block of the sequence, flash_attention_varlen.py:74-77).
+// Persistent, one CTA per SM (192 KB of tiles in shared memory, all 512 TMEM
+// columns).  A work item is a PAIR of 128-row query tiles that read the same
+// K/V rows: two query heads of one kv head at the same positions (GQA group
+// even), or two consecutive row tiles of one head (group odd).  Each 128-key
+// K/V tile is loaded once for both.  The two tiles ping-pong: while the
+// softmax warps of one tile work on its scores, the tensor core computes the
+// other tile's P.V and next S.
+//   warps 0-3 / 4-7  softmax of tile 0 / tile 1: thread r owns query row r
+//               (TMEM lane r); it loads its 128 scores with tcgen05.ld, applies
+//               the causal / length mask, updates the running max (base 2) and
+//               sum in fp32, and writes P as packed bf16 pairs over the first
+//               64 columns of the same score buffer (tcgen05.st).  Its O row
+//               is rescaled only when the running max grew by more than 2^8
+//               (otherwise the stale max keeps every P <= 2^8).  After the
+//               item's last tile the same warps normalise O and store it.
+//   warp 8      MMA issuer (one thread): S_t = Q_t.K^T (M=128, N=128, K=16
+//               per instruction, 8 instructions), O_t += P_t.V (M=128,
+//               N=128, 8 instructions) with P_t read from TMEM; each group
+//               ends with tcgen05.commit on an mbarrier.
+//   warp 9      TMA producer: lane 0 takes the work items and loads both Q
+//               tiles and the K tiles (2-stage ring), lane 1 the V tiles.
+// Every CTA builds the same work list in shared memory: only the non-empty
+// items, sequence-major (longest sequence first), heaviest tile first within
+// a sequence; items are taken from a global counter (dynamic balance) or,
+// without one, in a fixed boustrophedon order.  KV tiles strictly above the
+// diagonal are never loaded (the reference computes every KV block of the
+// sequence, flash_attention_varlen.py:74-77).
 //
 // Operand layouts (UMMA canonical forms):
-//   Q (128 x 128 d), K (64 x 128 d)  K-major, 128B swizzle: two blocks of
+//   Q (128 x 128 d), K (128 x 128 d)  K-major, 128B swizzle: two blocks of
 //         [row][64 d]; descriptor SBO = 1024 B (8 rows), start += 32 B per K
 //         step inside a block, += block size between blocks.
 //   P     A operand in TMEM: lane = query row, column c = keys 2c, 2c+1.
-//   V (64 keys x 128 d)  MN-major (d contiguous), 128B swizzle: LBO = 8 KB
+//   V (128 keys x 128 d)  MN-major (d contiguous), 128B swizzle: LBO = 16 KB
 //         between the two 64-d blocks, SBO = 1024 B (8 keys), start += 2 KB
 //         (16 keys) per K step.
-//   TMEM  columns [0,64) S0/P0, [64,128) S1/P1, [128,256) O; lane = query row.
-// MMAs issued by the one MMA thread execute in order, so S(j+2) overwriting
-// buffer j&1 follows the P.V that read P(j) from it.
+//   TMEM  columns [0,128) S0/P0, [128,256) S1/P1, [256,384) O0, [384,512) O1;
+//         lane = query row.
+// MMAs issued by the one MMA thread execute in order, so S_t(j+1) overwriting
+// P_t(j) follows the P_t(j).V that read it, and the commit that announces
+// S_t(j+1) also covers that P.V (O_t is stable while its softmax rescales it).
 // Every mbarrier wait is bounded; TMEM is always freed before the CTA exits.
 #include <math.h>
 
@@ -52,33 +55,37 @@
 namespace {
 
 constexpr int kD = 128;
-constexpr int kBM = 128;
-constexpr int kBN = 64;
-constexpr int kStages = 2;
-constexpr int kQBytes = kBM * kD * 2;       // 32 KB
+constexpr int kBM = 128;                    // query rows per tile (one TMEM lane each)
+constexpr int kBN = 128;                    // keys per K/V tile
+constexpr int kStages = 2;                  // K (and V) tile ring depth
+constexpr int kQBytes = kBM * kD * 2;       // 32 KB per Q tile
 constexpr int kQBlock = kQBytes / 2;        // 16 KB: [128 rows][64 d] swizzled block
-constexpr int kKVBytes = kBN * kD * 2;      // 16 KB per K (or V) tile
-constexpr int kKVBlock = kKVBytes / 2;      // 8 KB: [64 rows][64 d]
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kKVBytes = kBN * kD * 2;      // 32 KB per K (or V) tile
+constexpr int kKVBlock = kKVBytes / 2;      // 16 KB: [128 keys][64 d]
+constexpr int kOffQ = 0;                    // Q of tile 0, then tile 1
+constexpr int kOffK = kOffQ + 2 * kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
-constexpr int kSmemTiles = kOffV + kStages * kKVBytes;  // 96 KB
+constexpr int kSmemTiles = kOffV + kStages * kKVBytes;  // 192 KB
 constexpr int kSmemBytes = kSmemTiles + 1024;
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS0 = 0, kColO = 2 * kBN;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
+constexpr int kMmaWarp = 8;
+constexpr int kProducerWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 2 * kBN;  // + tile * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Of every kExpFmaPeriod columns, the first 2 * FMA_PAIRS (kernel template
-// parameter) use ex2_fma; the rest use the special-function unit.
-constexpr int kExpFmaPeriod = 8;
+// parameter) use the FMA-pipe exp2; the rest use the special-function unit.
+// In isolation a quarter on the FMA pipe is fastest, but inside this kernel
+// the extra instructions delay the MMA warp that shares their SM sub-partition,
+// so the default keeps every exponential on the special-function unit.
+constexpr int kExpFmaPeriod = 16;
 constexpr int kDefaultExpFmaPairs = 0;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxSeqs = 256;               // sequences per launch (the host splits larger batches)
-constexpr int kMaxTiles = 2048;             // 128-query tiles per sequence (max_seqlen <= 262144)
+constexpr int kMaxTiles = 2048;             // 128-row tiles per sequence (max_seqlen <= 262144)
 constexpr int kRing = 4;                    // item-index ring between the scheduler and the roles
-constexpr int kRingConsumers = 2 + 128;     // V lane, MMA thread, softmax threads
+constexpr int kRingConsumers = 2 + kSoftmaxThreads;  // V lane, MMA thread, softmax threads
 
 struct PrefillArgs {
   const int32_t* cu;
@@ -86,22 +93,24 @@ struct PrefillArgs {
   __nv_bfloat16* out;
   int64_t o_t, o_h;
   int num_seqs, num_heads, group, max_seqlen, zero_pad, total_tokens;
-  int n_tiles;          // ceil(max_seqlen / 128)
+  int pair_heads;       // 1: an item is query heads 2p, 2p+1 (group even); 0: two row tiles
   float scale_log2;
   int32_t* dev_status;
   int32_t* sched;       // nullable: [0] next item, [1] CTAs done (zero at launch, reset at exit)
 };
 
 // Work list shared by every CTA (each CTA builds the same one in shared
-// memory): the non-empty (tile, sequence, head) items, heaviest first -- tile
-// index descending (tile m attends to about 2m+2 K/V tiles of 64 keys),
-// sequences in descending order of their tile count, so the sequences that
-// reach tile m are a prefix of the sorted order.
+// memory): the non-empty items, sequence-major -- sequences in descending
+// order of their tile count, within a sequence the heaviest tiles first (a
+// tile at row m0 attends to m0/128 + 1 K/V tiles), within a step the head
+// pairs (or heads) in order.  The CTAs working at any moment then read the
+// K/V of one or two sequences, which stay in L2, and the list still ends with
+// its lightest items.
 struct WorkList {
   int len[kMaxSeqs];
   int start[kMaxSeqs];
   uint32_t key[kMaxSeqs];        // sorted: (kMaxTiles - 1 - tiles) << 16 | sequence
-  int prefix[kMaxTiles + 1];     // items before step u (tile n_tiles - 1 - u)
+  int seq_prefix[kMaxSeqs + 1];  // items before the r-th sequence of the sorted order
   int pad_prefix[kMaxSeqs + 1];  // padded adapter: zero rows before sequence s (all heads)
   unsigned char pad_ok[kMaxSeqs];  // rows [len, max_seqlen) of sequence s lie inside the output
   int n_items;
@@ -109,42 +118,60 @@ struct WorkList {
 };
 
 struct Item {
-  int start, len, m0, h, hk, n_kv;
+  int start, len, hk, n_kv;
+  int h[2], m0[2];  // query head and first row of tile 0 / tile 1
 };
 
+// Steps (heaviest first) a sequence of `tiles` row tiles contributes, and the
+// items per step.
+B200_DEVICE int seq_steps(const PrefillArgs& a, int tiles) {
+  return a.pair_heads ? tiles : (tiles + 1) / 2;
+}
+B200_DEVICE int items_per_step(const PrefillArgs& a) {
+  return a.pair_heads ? a.num_heads / 2 : a.num_heads;
+}
+
 B200_DEVICE Item decode_item(const PrefillArgs& a, const WorkList& W, int k) {
-  int lo = 0, hi = a.n_tiles;  // step u: largest with prefix[u] <= k
+  int lo = 0, hi = a.num_seqs;  // rank: largest with seq_prefix[rank] <= k
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (W.prefix[mid] <= k) lo = mid; else hi = mid;
+    if (W.seq_prefix[mid] <= k) lo = mid; else hi = mid;
   }
-  const int rem = k - W.prefix[lo];
-  const int rank = rem / a.num_heads;
+  const int per = items_per_step(a);
+  const int rem = k - W.seq_prefix[lo];
+  const int step = rem / per;
+  const int p = rem - step * per;
+  const uint32_t key = W.key[lo];
+  const int seq = static_cast<int>(key & 0xFFFFu);
+  const int tiles = kMaxTiles - 1 - static_cast<int>(key >> 16);
   Item it;
-  it.h = rem - rank * a.num_heads;
-  it.hk = it.h / a.group;
-  const int seq = static_cast<int>(W.key[rank] & 0xFFFFu);
   it.start = W.start[seq];
   it.len = W.len[seq];
-  it.m0 = (a.n_tiles - 1 - lo) * kBM;
-  it.n_kv = (min(it.len, it.m0 + kBM) + kBN - 1) / kBN;  // causal: keys < m0 + 128
+  if (a.pair_heads) {
+    it.h[0] = 2 * p;
+    it.h[1] = 2 * p + 1;
+    it.m0[0] = it.m0[1] = (tiles - 1 - step) * kBM;
+  } else {
+    it.h[0] = it.h[1] = p;
+    it.m0[0] = (seq_steps(a, tiles) - 1 - step) * 2 * kBM;
+    it.m0[1] = it.m0[0] + kBM;  // may lie past the sequence: computed, never stored
+  }
+  it.hk = it.h[0] / a.group;
+  it.n_kv = (min(it.len, it.m0[1] + kBM) + kBN - 1) / kBN;  // causal: keys < m0 + 128
   return it;
 }
 
 // Every barrier below completes once per use of its slot.  A waiter asks for
-// the n-th completion with parity (n >> 1) & 1 of slot n & 1 (or parity n & 1
-// for single-slot barriers); the pipeline order guarantees that slot has not
-// run two completions ahead of any waiter, so parities are unambiguous.
+// the c-th completion of a slot with parity c & 1; the pipeline order
+// guarantees that no slot runs two completions ahead of any of its waiters.
 struct __align__(8) Barriers {
-  uint64_t q_full, q_empty;   // Q tile loaded / all S of its item issued and done
-  uint64_t k_full[kStages];
-  uint64_t v_full[kStages];
-  uint64_t k_empty[kStages];  // K stage free: its S = Q.K^T finished
-  uint64_t v_empty[kStages];  // V stage free: its P.V finished
-  uint64_t s_full[2];         // S(g) in TMEM buffer g & 1
-  uint64_t p_full[2];         // P(g) written over S(g)
-  uint64_t pv_done[2];        // P(g).V(g) finished
-  uint64_t o_free;            // the item's O was read by the softmax warps
+  uint64_t q_full, q_empty;   // both Q tiles loaded / every S of the item done
+  uint64_t k_full[kStages], k_empty[kStages];  // K tile loaded / both S that read it done
+  uint64_t v_full[kStages], v_empty[kStages];  // V tile loaded / both P.V that read it done
+  uint64_t s_full[2];         // S_t(g) in TMEM (every earlier MMA of the CTA done too)
+  uint64_t p_full[2];         // P_t(g) written over S_t(g), O_t rescaled
+  uint64_t o_done[2];         // the item's last P_t.V done (O_t final)
+  uint64_t o_free[2];         // the item's O_t was read by its softmax warps
   uint64_t ring_full[kRing], ring_empty[kRing];
   uint32_t tmem_base;
   int32_t error;
@@ -246,6 +273,16 @@ B200_DEVICE void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+B200_DEVICE void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 B200_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 B200_DEVICE void mbar_arrive(uint32_t bar) {
@@ -305,16 +342,13 @@ B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
     }
   }
   if (threadIdx.x == 0) {
-    // prefix over steps u (tile m = n_tiles - 1 - u): sequences with more than
-    // m tiles are the first `cnt` of the sorted order
-    int cnt = 0, acc = 0;
-    for (int u = 0; u < a.n_tiles; ++u) {
-      const int m = a.n_tiles - 1 - u;
-      while (cnt < n && static_cast<int>(kMaxTiles - 1 - (W.key[cnt] >> 16)) > m) ++cnt;
-      W.prefix[u] = acc;
-      acc += cnt * a.num_heads;
+    const int per = items_per_step(a);
+    int acc = 0;
+    for (int r = 0; r < n; ++r) {
+      W.seq_prefix[r] = acc;
+      acc += seq_steps(a, kMaxTiles - 1 - static_cast<int>(W.key[r] >> 16)) * per;
     }
-    W.prefix[a.n_tiles] = acc;
+    W.seq_prefix[n] = acc;
     W.n_items = acc;
     int pad = 0;
     for (int s2 = 0; s2 < n; ++s2) {
@@ -327,7 +361,7 @@ B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
 }
 
 template <int FMA_PAIRS>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     varlen_prefill_kernel(const __grid_constant__ CUtensorMap tmq,
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv, const PrefillArgs a) {
@@ -353,13 +387,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_q = b200::smem_u32(&B.q_full);
   const uint32_t bar_qe = b200::smem_u32(&B.q_empty);
   auto bar_k = [&](int s) { return b200::smem_u32(&B.k_full[s]); };
-  auto bar_v = [&](int s) { return b200::smem_u32(&B.v_full[s]); };
   auto bar_ke = [&](int s) { return b200::smem_u32(&B.k_empty[s]); };
+  auto bar_v = [&](int s) { return b200::smem_u32(&B.v_full[s]); };
   auto bar_ve = [&](int s) { return b200::smem_u32(&B.v_empty[s]); };
-  auto bar_sf = [&](int g) { return b200::smem_u32(&B.s_full[g & 1]); };
-  auto bar_p = [&](int g) { return b200::smem_u32(&B.p_full[g & 1]); };
-  auto bar_o = [&](int g) { return b200::smem_u32(&B.pv_done[g & 1]); };
-  const uint32_t bar_of = b200::smem_u32(&B.o_free);
+  auto bar_sf = [&](int t) { return b200::smem_u32(&B.s_full[t]); };
+  auto bar_p = [&](int t) { return b200::smem_u32(&B.p_full[t]); };
+  auto bar_od = [&](int t) { return b200::smem_u32(&B.o_done[t]); };
+  auto bar_of = [&](int t) { return b200::smem_u32(&B.o_free[t]); };
   auto bar_rf = [&](int n) { return b200::smem_u32(&B.ring_full[n & (kRing - 1)]); };
   auto bar_re = [&](int n) { return b200::smem_u32(&B.ring_empty[n & (kRing - 1)]); };
 
@@ -368,16 +402,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     b200::mbar_init(bar_qe, 1);
     for (int s = 0; s < kStages; ++s) {
       b200::mbar_init(bar_k(s), 1);
-      b200::mbar_init(bar_v(s), 1);
       b200::mbar_init(bar_ke(s), 1);
+      b200::mbar_init(bar_v(s), 1);
       b200::mbar_init(bar_ve(s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      b200::mbar_init(bar_sf(s), 1);
-      b200::mbar_init(bar_p(s), 128);
-      b200::mbar_init(bar_o(s), 1);
+    for (int t = 0; t < 2; ++t) {
+      b200::mbar_init(bar_sf(t), 1);
+      b200::mbar_init(bar_p(t), 128);
+      b200::mbar_init(bar_od(t), 1);
+      b200::mbar_init(bar_of(t), 128);
     }
-    b200::mbar_init(bar_of, 128);
     for (int r = 0; r < kRing; ++r) {
       b200::mbar_init(bar_rf(r), 1);
       b200::mbar_init(bar_re(r), kRingConsumers);
@@ -406,8 +440,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
 
   if (warp == kProducerWarp) {
-    // lane 0 streams Q and the K tiles, lane 1 the V tiles: a K stage is
-    // refilled as soon as its S = Q.K^T is done, without waiting for P.V
+    // lane 0: scheduler, both Q tiles and the K tiles; lane 1: the V tiles.
+    // A K (V) stage is refilled once both S (both P.V) that read it are done.
     if (lane == 0) {
       b200::prefetch_tensormap(&tmq);
       b200::prefetch_tensormap(&tmk);
@@ -419,7 +453,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int round = n / static_cast<int>(gridDim.x);
         int k = a.sched != nullptr
                     ? atomicAdd(&a.sched[0], 1)
-                    : round * gridDim.x + ((round & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+                    : round * static_cast<int>(gridDim.x) +
+                          ((round & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
         if (k >= W.n_items) k = -1;
         if (n >= kRing && !(ok = wait_or_flag(bar_re(n), ((n / kRing) - 1) & 1, &B, a.dev_status)))
           break;
@@ -428,12 +463,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (k < 0) break;
         const Item it = decode_item(a, W, k);
         if (n > 0 && !(ok = wait_or_flag(bar_qe, (n - 1) & 1, &B, a.dev_status))) break;
-        b200::mbar_arrive_expect_tx(bar_q, kQBytes);
-        b200::tma_load_3d(sQ, &tmq, bar_q, 0, it.h, it.start + it.m0);
-        b200::tma_load_3d(sQ + kQBlock, &tmq, bar_q, 64, it.h, it.start + it.m0);
+        b200::mbar_arrive_expect_tx(bar_q, 2 * kQBytes);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t dq = sQ + t * kQBytes;
+          b200::tma_load_3d(dq, &tmq, bar_q, 0, it.h[t], it.start + it.m0[t]);
+          b200::tma_load_3d(dq + kQBlock, &tmq, bar_q, 64, it.h[t], it.start + it.m0[t]);
+        }
         for (int j = 0; j < it.n_kv; ++j, ++kc) {
           const int s = kc & 1;
-          if (kc >= kStages && !(ok = wait_or_flag(bar_ke(s), ((kc >> 1) - 1) & 1, &B, a.dev_status)))
+          if (kc >= kStages &&
+              !(ok = wait_or_flag(bar_ke(s), ((kc >> 1) - 1) & 1, &B, a.dev_status)))
             break;
           const uint32_t dk = sK + s * kKVBytes;
           b200::mbar_arrive_expect_tx(bar_k(s), kKVBytes);
@@ -451,7 +491,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const Item it = decode_item(a, W, k);
         for (int j = 0; j < it.n_kv; ++j, ++vc) {
           const int s = vc & 1;
-          if (vc >= kStages && !(ok = wait_or_flag(bar_ve(s), ((vc >> 1) - 1) & 1, &B, a.dev_status)))
+          if (vc >= kStages &&
+              !(ok = wait_or_flag(bar_ve(s), ((vc >> 1) - 1) & 1, &B, a.dev_status)))
             break;
           const uint32_t dv = sV + s * kKVBytes;
           b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
@@ -464,68 +505,82 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(kBN, false);
       constexpr uint32_t idO = idesc_bf16(kD, true);
-      int g0 = 0;  // g = global index of S / P / P.V products in this CTA
+      // S_t = Q_t . K(s)^T into tile t's score buffer
+      auto issue_s = [&](int t, int s) {
+        const uint32_t q = sQ + t * kQBytes, kt = sK + s * kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t inblk = (kk & 3) * 32;
+          umma_bf16(tmem + kColS + t * kBN, smem_desc(q + (kk >> 2) * kQBlock + inblk, 16, 1024),
+                    smem_desc(kt + (kk >> 2) * kKVBlock + inblk, 16, 1024), idS,
+                    kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_sf(t));
+      };
+      // O_t (+)= P_t . V(s), P_t read from tile t's score buffer in TMEM
+      auto issue_pv = [&](int t, int s, bool accumulate) {
+        const uint32_t vt = sV + s * kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          umma_bf16_ts(tmem + kColO + t * kD, tmem + kColS + t * kBN + kk * 8,
+                       smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
+                       (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+      int g = 0;  // K/V tiles consumed by this CTA before the current item
       bool ok = true;
-      for (int n_item = 0; ok; ++n_item) {
-        const int k = next_item(n_item, ok);
+      for (int n = 0; ok; ++n) {
+        const int k = next_item(n, ok);
         if (!ok || k < 0) break;
         const Item it = decode_item(a, W, k);
-        if (!(ok = wait_or_flag(bar_q, n_item & 1, &B, a.dev_status))) break;
+        if (!(ok = wait_or_flag(bar_q, n & 1, &B, a.dev_status))) break;
         tc_fence_after();
-        for (int j = 0; j <= it.n_kv; ++j) {
-          if (j < it.n_kv) {
-            // ---- S(g) = Q . K^T into buffer g & 1 (it last held P(g-2), whose
-            // P.V was issued before this point; MMAs execute in issue order)
-            const int g = g0 + j;
-            const int s = g & 1;
-            if (!(ok = wait_or_flag(bar_k(s), (g >> 1) & 1, &B, a.dev_status))) break;
-            tc_fence_after();
-            const uint32_t dS = tmem + kColS0 + s * kBN;
-            const uint32_t kt = sK + s * kKVBytes;
-#pragma unroll
-            for (int kk = 0; kk < kD / 16; ++kk) {
-              const uint32_t inblk = (kk & 3) * 32;
-              umma_bf16(dS, smem_desc(sQ + (kk >> 2) * kQBlock + inblk, 16, 1024),
-                        smem_desc(kt + (kk >> 2) * kKVBlock + inblk, 16, 1024), idS,
-                        kk > 0 ? 1u : 0u);
+        // step j issues P_t(j-1).V(j-1) then S_t(j) for t = 0, 1: S_t(j)
+        // overwrites P_t(j-1), so its P.V goes first (MMAs run in order)
+        for (int j = 0; ok && j <= it.n_kv; ++j) {
+          const int gs = g + j, gp = gs - 1;  // tile of S(j) / of P(j-1)
+          for (int t = 0; t < 2; ++t) {
+            if (j > 0) {
+              if (t == 0 && !(ok = wait_or_flag(bar_v(gp & 1), (gp >> 1) & 1, &B, a.dev_status)))
+                break;
+              if (!(ok = wait_or_flag(bar_p(t), gp & 1, &B, a.dev_status))) break;
+              if (j == 1 && n > 0 &&
+                  !(ok = wait_or_flag(bar_of(t), (n - 1) & 1, &B, a.dev_status)))
+                break;
+              tc_fence_after();
+              issue_pv(t, gp & 1, j > 1);
+              if (j == it.n_kv) umma_commit(bar_od(t));
             }
-            umma_commit(bar_sf(g));
-            umma_commit(bar_ke(s));
+            if (j < it.n_kv) {
+              if (t == 0 && !(ok = wait_or_flag(bar_k(gs & 1), (gs >> 1) & 1, &B, a.dev_status)))
+                break;
+              tc_fence_after();
+              issue_s(t, gs & 1);
+            }
+          }
+          if (!ok) break;
+          if (j < it.n_kv) {
+            umma_commit(bar_ke(gs & 1));
             if (j == it.n_kv - 1) umma_commit(bar_qe);
           }
-          if (j >= 1) {
-            // ---- O += P(g) . V(g), P from TMEM
-            const int g = g0 + j - 1;
-            const int s = g & 1;
-            if (!(ok = wait_or_flag(bar_p(g), (g >> 1) & 1, &B, a.dev_status))) break;
-            if (!(ok = wait_or_flag(bar_v(s), (g >> 1) & 1, &B, a.dev_status))) break;
-            if (j == 1 && n_item > 0 &&
-                !(ok = wait_or_flag(bar_of, (n_item - 1) & 1, &B, a.dev_status)))
-              break;
-            tc_fence_after();
-            const uint32_t vt = sV + s * kKVBytes;
-#pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              umma_bf16_ts(tmem + kColO, tmem + kColS0 + s * kBN + kk * 8,
-                           smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
-                           (j > 1 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(bar_o(g));
-            umma_commit(bar_ve(s));
-          }
+          if (j > 0) umma_commit(bar_ve(gp & 1));
         }
-        g0 += it.n_kv;
+        g += it.n_kv;
       }
     }
   } else {
     // ---------------------------------------------------------- softmax
-    const int r = threadIdx.x;  // query row in the tile == TMEM lane
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    const int t = warp >> 2;            // tile of this warpgroup
+    const int r = threadIdx.x & 127;    // query row in the tile == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t sbuf = tmem + lane_addr + kColS + t * kBN;
+    const uint32_t obuf = tmem + lane_addr + kColO + t * kD;
 
     // padded adapter: zero the rows past every sequence (spread over all CTAs)
     if (a.zero_pad) {
       const int total = W.pad_prefix[a.num_seqs];
-      for (int z = blockIdx.x * 128 + r; z < total; z += gridDim.x * 128) {
+      for (int z = blockIdx.x * kSoftmaxThreads + threadIdx.x; z < total;
+           z += gridDim.x * kSoftmaxThreads) {
         int lo = 0, hi = a.num_seqs;
         while (hi - lo > 1) {
           const int mid = (lo + hi) >> 1;
@@ -543,30 +598,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
 
-    int g0 = 0;
+    int g = 0;
     bool ok = true;
     for (int n = 0; ok; ++n) {
       const int k = next_item(n, ok);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || k < 0) break;
       const Item it = decode_item(a, W, k);
-      const int qpos = it.m0 + r;  // position within the sequence
+      const int qpos = it.m0[t] + r;  // position within the sequence
       float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.n_kv; ++j) {
-        const int g = g0 + j;
-        const int s = g & 1;
-        ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(g), (g >> 1) & 1, &B, a.dev_status));
+      for (int j = 0; j < it.n_kv; ++j, ++g) {
+        ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(t), g & 1, &B, a.dev_status));
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sbuf = tmem + lane_addr + kColS0 + s * kBN;
         uint32_t xs[kBN];
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) tmem_ld32(sbuf + c * 32, xs + c * 32);
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld(xs + c * 32);
-        float x[kBN];
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) x[c] = __uint_as_float(xs[c]);
+        float* x = reinterpret_cast<float*>(xs);
 
         const int n0 = j * kBN;
         if (n0 + kBN - 1 > qpos || n0 + kBN > it.len) {
@@ -575,14 +625,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < kBN; ++c)
             if (c >= lim) x[c] = -INFINITY;
         }
-        // tree max (8 independent chains)
+        // tree max (8 independent chains of 3-input max)
         float mq[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) mq[e] = x[e];
+        for (int e = 0; e < 8; ++e) mq[e] = b200::fmax3(x[e], x[e + 8], x[e + 16]);
 #pragma unroll
-        for (int c = 8; c < kBN; ++c) mq[c & 7] = fmaxf(mq[c & 7], x[c]);
-        const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
-                               fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))) *
+        for (int c = 24; c + 16 <= kBN - 8; c += 16)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mq[e] = b200::fmax3(mq[e], x[c + e], x[c + e + 8]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mq[e] = fmaxf(mq[e], x[kBN - 8 + e]);
+        const float mx = b200::fmax3(b200::fmax3(mq[0], mq[1], mq[2]),
+                                     b200::fmax3(mq[3], mq[4], mq[5]), fmaxf(mq[6], mq[7])) *
                          a.scale_log2;
         float alpha = 1.f;
         bool rescale = false;
@@ -593,66 +647,73 @@ __global__ void __launch_bounds__(kThreads, 2)
           m_used = mx;
           rescale = true;
         }
-        float sq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[kBN / 2];
+        // p = 2^(x * scale_log2 - m) on packed pairs; of every 16 columns the
+        // first 2 * FMA_PAIRS take the FMA-pipe exp2, the rest the MUFU
+        const uint64_t sc2 = b200::f2_pack(a.scale_log2, a.scale_log2);
+        const uint64_t nm2 = b200::f2_pack(-m_used, -m_used);
+        uint64_t sq[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int c = 0; c < kBN; c += 2) {
-          // a fixed share of the exponentials runs on the FMA pipe
-          const bool fma_pair = (c & (kExpFmaPeriod - 1)) < FMA_PAIRS * 2;
-          const float y0 = fmaf(x[c], a.scale_log2, -m_used);
-          const float y1 = fmaf(x[c + 1], a.scale_log2, -m_used);
-          const float p0 = fma_pair ? b200::ex2_fma(y0) : b200::ex2(y0);
-          const float p1 = fma_pair ? b200::ex2_fma(y1) : b200::ex2(y1);
-          sq[(c >> 1) & 7] += p0 + p1;
-          pk[c / 2] = b200::pack_bf16x2(p0, p1);
+        for (int h = 0; h < kBN / 32; ++h) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const uint64_t y = b200::f2_fma(b200::f2_pack(x[h * 32 + c], x[h * 32 + c + 1]), sc2, nm2);
+            float p0, p1;
+            if ((c & (kExpFmaPeriod - 1)) < FMA_PAIRS * 2) {
+              b200::f2_unpack(b200::ex2_fma2(y), p0, p1);
+            } else {
+              float y0, y1;
+              b200::f2_unpack(y, y0, y1);
+              p0 = b200::ex2(y0);
+              p1 = b200::ex2(y1);
+            }
+            sq[(c >> 1) & 3] = b200::f2_add(sq[(c >> 1) & 3], b200::f2_pack(p0, p1));
+            pk[c / 2] = b200::pack_bf16x2(p0, p1);
+          }
+          // P over the first half of its own score buffer (S is in registers)
+          tmem_st16(sbuf + h * 16, pk);
         }
-        const float rowsum =
-            ((sq[0] + sq[1]) + (sq[2] + sq[3])) + ((sq[4] + sq[5]) + (sq[6] + sq[7]));
+        float s0, s1;
+        b200::f2_unpack(b200::f2_add(b200::f2_add(sq[0], sq[1]), b200::f2_add(sq[2], sq[3])), s0, s1);
+        const float rowsum = s0 + s1;
 
-        // P(g) over the first half of its own score buffer (S(g) is consumed)
-        tmem_st32(sbuf, pk);
         if (__any_sync(0xffffffffu, rescale)) {
-          // O must hold everything up to P(g-1).V(g-1) before it is rescaled;
-          // tcgen05.ld/st are warp-collective, so the warp's rows rescale
-          // together (alpha == 1 for rows whose max did not move)
-          ok = __all_sync(0xffffffffu, wait_or_flag(bar_o(g - 1), ((g - 1) >> 1) & 1, &B,
-                                                    a.dev_status));
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
+          // S_t(g) done implies every earlier P_t.V is done, and the next one
+          // waits for this warp's arrival: O_t is stable here.  tcgen05.ld/st
+          // are warp-collective, so the warp's rows rescale together (alpha ==
+          // 1 for rows whose max did not move)
+#pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             uint32_t rr[32];
-            tmem_ld32(tmem + lane_addr + kColO + c * 32, rr);
+            tmem_ld32(obuf + c * 32, rr);
             tmem_wait_ld(rr);
 #pragma unroll
             for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-            tmem_st32(tmem + lane_addr + kColO + c * 32, rr);
+            tmem_st32(obuf + c * 32, rr);
           }
         }
         l = l * alpha + rowsum;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p(g));
+        mbar_arrive(bar_p(t));
       }
       if (!ok) break;
 
-      // ---- epilogue: O / l -> bf16 rows; O is released before the stores
-      const int glast = g0 + it.n_kv - 1;
-      ok = __all_sync(0xffffffffu,
-                      wait_or_flag(bar_o(glast), (glast >> 1) & 1, &B, a.dev_status));
+      // ---- epilogue: O_t / l -> bf16 rows; O_t is released before the stores
+      ok = __all_sync(0xffffffffu, wait_or_flag(bar_od(t), n & 1, &B, a.dev_status));
       if (!ok) break;
       tc_fence_after();
       uint32_t ov[kD];
 #pragma unroll
-      for (int c = 0; c < kD / 32; ++c) tmem_ld32(tmem + lane_addr + kColO + c * 32, ov + c * 32);
+      for (int c = 0; c < kD / 32; ++c) tmem_ld32(obuf + c * 32, ov + c * 32);
 #pragma unroll
       for (int c = 0; c < kD / 32; ++c) tmem_wait_ld(ov + c * 32);
       tc_fence_before();
-      mbar_arrive(bar_of);
+      mbar_arrive(bar_of(t));
       if (qpos < it.len) {  // rows past the sequence are zeroed by the pass above
         const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
-                              static_cast<int64_t>(it.h) * a.o_h;
+                              static_cast<int64_t>(it.h[t]) * a.o_h;
 #pragma unroll
         for (int e = 0; e < kD; e += 8) {
           uint4 v;
@@ -663,7 +724,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           *reinterpret_cast<uint4*>(orow + e) = v;
         }
       }
-      g0 += it.n_kv;
     }
   }
 
@@ -795,11 +855,11 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
     a.max_seqlen = max_seqlen;
     a.zero_pad = zero_pad_rows != 0;
     a.total_tokens = total_tokens;
-    a.n_tiles = n_tiles;
+    a.pair_heads = (a.group % 2) == 0 ? 1 : 0;
     a.scale_log2 = scale * kLog2e;
     a.dev_status = dev_status;
     a.sched = work_counter;
-    dim3 grid(static_cast<unsigned>(2 * sms));  // two persistent CTAs per SM
+    dim3 grid(static_cast<unsigned>(sms));  // one persistent CTA per SM
     switch (pairs) {
       case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
       case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
