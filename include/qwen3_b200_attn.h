@@ -114,12 +114,17 @@ int b200_kv_scatter_slots(const void* k, const void* v,
 /*
  * Split-K paged decode: workspace bytes needed for `batch` requests, `num_heads`
  * query heads and a block table `max_pages` wide, with `pages_per_split`
- * pages per split (<= 0 selects the library default).  Depends on shapes only.
+ * pages per split.  <= 0 returns enough for any split the library may pick by
+ * default (pass b200_paged_decode_default_split(...) to size it exactly).
+ * Depends on shapes only.
  */
 size_t b200_paged_decode_workspace_size(int batch, int num_heads, int max_pages,
                                         int pages_per_split);
 
-/* The split size the library picks for these shapes when pages_per_split <= 0. */
+/* The split size the library picks for these shapes when pages_per_split <= 0:
+ * large splits (up to 128 pages), but enough CTAs for about 4 per SM when the
+ * sequences fill half of the block table (depends on the current device's SM
+ * count). */
 int b200_paged_decode_default_split(int batch, int num_kv_heads, int max_pages);
 
 /*

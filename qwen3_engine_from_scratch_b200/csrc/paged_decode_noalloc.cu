@@ -62,6 +62,8 @@ extern "C" int b200_paged_decode_noalloc(const void* q, int64_t q_stride_b, int6
                                          int num_blocks, int max_pages, int max_requests,
                                          float scale, int pages_per_split, int32_t* dev_status,
                                          void* stream) {
+  if (pages_per_split <= 0 && batch > 0 && num_kv_heads > 0 && max_pages > 0)
+    pages_per_split = b200_paged_decode_default_split(batch, num_kv_heads, max_pages);
   const size_t need =
       b200_paged_decode_workspace_size(batch, num_heads, max_pages, pages_per_split);
   if (need > kNoAllocScratchBytes) return B200_ERR_WORKSPACE;  // beyond the static maximum

@@ -221,6 +221,18 @@ def decode_workspace_bytes(batch, num_heads, max_pages, pages_per_split=0) -> in
                                                                pages_per_split))
 
 
+_split_cache: dict[tuple[int, int, int, int], int] = {}
+
+
+def _default_split(lib, batch, num_kv_heads, max_pages) -> int:
+    key = (torch.cuda.current_device(), batch, num_kv_heads, max_pages)
+    v = _split_cache.get(key)
+    if v is None:
+        v = int(lib.b200_paged_decode_default_split(batch, num_kv_heads, max_pages))
+        _split_cache[key] = v
+    return v
+
+
 def paged_decode(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, scale,
                  out=None, pages_per_split=0):
     """Split-K paged decode on one layer view of the pool.
@@ -244,6 +256,8 @@ def paged_decode(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, scale
         out = torch.empty((B, H, D), dtype=torch.bfloat16, device=q.device)
     max_pages = block_table_2d.shape[1]
     lib = _native.load()
+    if pages_per_split <= 0:
+        pages_per_split = _default_split(lib, B, Hkv, max_pages)
     ws_bytes = lib.b200_paged_decode_workspace_size(B, H, max_pages, pages_per_split)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     st = lib.b200_paged_decode(

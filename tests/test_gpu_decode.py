@@ -186,7 +186,8 @@ def test_config2_shape_vs_oracle(H, Hkv, cuda, native_lib):
 
 def test_batch_permutation_and_split_invariance(cuda, native_lib):
     """Size-independent properties at full config-2 size: permuting the batch
-    permutes the output bit-exactly; two half batches equal one full batch."""
+    permutes the output bit-exactly; two half batches equal one full batch at
+    the same split size (the default split depends on the batch size)."""
     import qwen3_engine_from_scratch_b200 as qb
     w = _c2_like(cuda, num_blocks=16384, seed=99)
     scale = 1 / math.sqrt(128)
@@ -194,8 +195,11 @@ def test_batch_permutation_and_split_invariance(cuda, native_lib):
     perm = torch.randperm(64, device=cuda)
     permuted = qb.paged_decode(w["q"][perm], w["kp"], w["vp"], w["bt"], w["seq"], w["rows"][perm], scale)
     assert torch.equal(permuted, full[perm])
-    a = qb.paged_decode(w["q"][:32], w["kp"], w["vp"], w["bt"], w["seq"], w["rows"][:32], scale)
-    b = qb.paged_decode(w["q"][32:], w["kp"], w["vp"], w["bt"], w["seq"], w["rows"][32:], scale)
+    pps = int(qb._native.load().b200_paged_decode_default_split(64, 8, w["bt"].shape[1]))
+    a = qb.paged_decode(w["q"][:32], w["kp"], w["vp"], w["bt"], w["seq"], w["rows"][:32], scale,
+                        pages_per_split=pps)
+    b = qb.paged_decode(w["q"][32:], w["kp"], w["vp"], w["bt"], w["seq"], w["rows"][32:], scale,
+                        pages_per_split=pps)
     assert torch.equal(torch.cat([a, b]), full)
 
 
