@@ -16,8 +16,9 @@ the reference-named API ``triton_paged_attention_decode_batch``.
 than L2 (126 MB), so no flush is needed between steps.  ``e2e`` repeats the
 step through the same public API with the step's q/k/v copied from pinned
 host memory and the outputs copied back inside the timed region.
-``roofline`` is for the decode kernels (split + merge) timed live with CUDA
-events around every decode call of the timed region.
+``roofline`` is for the decode kernel (splits merged in-kernel by the last
+split of each request x kv head) timed live with CUDA events around every
+decode call of the timed region.
 
 Multi-GPU: one process per GPU (torchrun), each rank owns its own requests,
 pool and block table -- no collective on the data path ("scaling": "weak").
@@ -257,8 +258,7 @@ def run_b200(args, rank, world, local_rank):
     scale = HEAD_DIM ** -0.5
     lens = np.asarray(w["lens"], dtype=np.int64)
     max_pages = pool.block_table_2d.shape[1]
-    n_splits = math.ceil(max_pages / max(1, qb._native.load().b200_paged_decode_default_split(B, Hkv, max_pages)))
-    launches_per_layer = 2 + (1 if n_splits > 1 else 0)
+    launches_per_layer = 2   # KV write + decode (the split merge runs inside the decode kernel)
 
     def layer_call(l):
         ops.kv_scatter_rows(k_new[l], v_new[l], pool.k_buffer, pool.v_buffer, pool.seq_lens,
@@ -381,7 +381,7 @@ def run_b200(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2),
                 "d2h_bytes_per_step": int(hout.numel() * 2),
                 "api": "triton_paged_attention_decode_batch (pinned host q/k/v in, host out)"},
-        "roofline": {"kernel": "paged_decode_split_kernel + paged_decode_merge_kernel",
+        "roofline": {"kernel": "paged_decode_split_kernel",
                      "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),

@@ -138,7 +138,13 @@ int b200_paged_decode_default_split(int batch, int num_kv_heads, int max_pages);
  * strides (block, head, slot) in elements, head_dim stride 1.
  * q strides (batch, head); out strides (batch, head).  fp32 softmax, bf16 out.
  * `workspace` must hold b200_paged_decode_workspace_size(...) bytes (16-byte
- * aligned); it carries the per-split partials between the two kernels.
+ * aligned) when that size is non-zero.  Its first 256 KiB are split-arrival
+ * counters (one per request x kv head, at most 65536 pairs): zero-fill the
+ * workspace once when it is allocated; every launch leaves the counters zero,
+ * so the same workspace serves later launches of any shape on one stream.
+ * The rest carries the per-split partials, merged by the last split of each
+ * (request, kv head) inside the same kernel.  Launches that may overlap on
+ * the GPU need separate workspaces.
  */
 int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                       const void* k_pool, const void* v_pool,

@@ -11,7 +11,10 @@
 //   A CTA has 4 warps.  Warp w takes pages w, w+4, ... of the split and keeps
 //   its own online-softmax state; the 4 states are merged in shared memory at
 //   the end.  A pair with one split writes the bf16 output directly; else the
-//   split writes an fp32 partial (m, l, acc) and a second kernel merges them.
+//   split writes an fp32 partial (m, l, acc) to the workspace and bumps the
+//   pair's arrival counter; the CTA that arrives last merges the partials
+//   (they are in L2) and writes the output, then zeroes the counter, so the
+//   counters are zero again after every launch.
 //
 // Data movement
 //   Each page of one kv head is a contiguous 16 x 128 bf16 tile (4 KB) of K
@@ -52,6 +55,11 @@ constexpr int kMinDefaultPagesPerSplit = 16;
 constexpr int kMaxPagesPerSplit = 32 * kWarps;  // a warp's page ids live one per lane
 constexpr int kSmemBytes = kWarps * kStages * kSlotBytes + 1024;
 constexpr float kLog2e = 1.4426950408889634f;
+// The workspace starts with one split-arrival counter per (request, kv head),
+// at a fixed place whatever the shapes, so one zeroed workspace can serve
+// launches of any shape; the partials follow.
+constexpr int kMaxPairs = 65536;
+constexpr size_t kCounterBytes = kMaxPairs * sizeof(int32_t);
 
 struct DecodeArgs {
   const __nv_bfloat16* q;
@@ -62,8 +70,9 @@ struct DecodeArgs {
   const int32_t* row_ids;
   __nv_bfloat16* out;
   int64_t o_b, o_h;
-  float* ws_acc;  // [batch][num_heads][max_splits][128]
-  float* ws_ml;   // [batch][num_heads][max_splits][2]
+  int32_t* ws_done;  // [batch * num_kv_heads] split arrivals (zero at launch, zero at exit)
+  float* ws_acc;     // [batch][num_heads][max_splits][128]
+  float* ws_ml;      // [batch][num_heads][max_splits][2]
   int batch, num_heads, num_kv_heads, group, num_blocks, max_pages, max_requests;
   int pages_per_split, max_splits;
   float scale_log2;
@@ -330,41 +339,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   }
-}
+  if (nsplit == 1) return;
 
-// One warp per (request, query head): merge the per-split partials.
-__global__ void __launch_bounds__(256) paged_decode_merge_kernel(const DecodeArgs a) {
-  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= static_cast<int64_t>(a.batch) * a.num_heads) return;
-  const int b = static_cast<int>(gw / a.num_heads);
-  const int hq = static_cast<int>(gw - static_cast<int64_t>(b) * a.num_heads);
-  int row, L, err;
-  const int npages = request_pages(a, b, row, L, err);
-  const int ns = (npages + a.pages_per_split - 1) / a.pages_per_split;
-  if (ns <= 1) return;  // written by the split kernel (or zero-filled there)
-
-  const int64_t base = (static_cast<int64_t>(b) * a.num_heads + hq) * a.max_splits;
-  const float* ml = a.ws_ml + base * 2;
-  const float4* accp = reinterpret_cast<const float4*>(a.ws_acc + base * kD) + lane;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  float l = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const float sc = b200::ex2(ml[2 * s] - M);
-    l += sc * ml[2 * s + 1];
-    const float4 v = accp[s * (kD / 4)];
-    o.x += sc * v.x;
-    o.y += sc * v.y;
-    o.z += sc * v.z;
-    o.w += sc * v.w;
+  // ---- arrival: the last split of the pair merges every partial of the pair
+  __shared__ int s_last;
+  __threadfence();  // this CTA's partials are visible device-wide before its arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(&a.ws_done[pair], 1);
+    s_last = prev == nsplit - 1;
+    if (s_last) {
+      __threadfence();             // order the partial reads after every arrival
+      a.ws_done[pair] = 0;         // no other CTA of this launch touches it again
+    }
   }
-  const float inv = 1.f / l;
-  uint2 packed;
-  packed.x = b200::pack_bf16x2(o.x * inv, o.y * inv);
-  packed.y = b200::pack_bf16x2(o.z * inv, o.w * inv);
-  *reinterpret_cast<uint2*>(a.out + b * a.o_b + hq * a.o_h + lane * 4) = packed;
+  __syncthreads();
+  if (!s_last) return;
+  for (int h = 0; h < G; ++h) {
+    const int hq = hkv * G + h;
+    const int64_t base = (static_cast<int64_t>(b) * a.num_heads + hq) * a.max_splits;
+    const float* ml = a.ws_ml + base * 2;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(ml + 2 * sp));
+    float o = 0.f, l = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float sc = b200::ex2(__ldcg(ml + 2 * sp) - M);
+      l += sc * __ldcg(ml + 2 * sp + 1);
+      o += sc * __ldcg(a.ws_acc + (base + sp) * kD + d);
+    }
+    a.out[b * a.o_b + hq * a.o_h + d] = __float2bfloat16(o / l);
+  }
 }
 
 bool mult8(int64_t s) { return (s & 7) == 0; }
@@ -415,7 +419,8 @@ extern "C" size_t b200_paged_decode_workspace_size(int batch, int num_heads, int
   if (pages_per_split <= 0) pages_per_split = kMinDefaultPagesPerSplit;
   const int ms = max_splits_for(max_pages, pages_per_split);
   if (ms <= 1) return 0;
-  return static_cast<size_t>(batch) * num_heads * ms * (kD + 2) * sizeof(float);
+  // the counters, then the partials
+  return kCounterBytes + static_cast<size_t>(batch) * num_heads * ms * (kD + 2) * sizeof(float);
 }
 
 extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
@@ -438,7 +443,7 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
   if (num_heads % num_kv_heads != 0) return B200_ERR_INVALID_ARGUMENT;
   const int G = num_heads / num_kv_heads;
   if (G > kMaxG) return B200_ERR_UNSUPPORTED;
-  if (static_cast<int64_t>(batch) * num_kv_heads > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(batch) * num_kv_heads > kMaxPairs) return B200_ERR_UNSUPPORTED;
   if (pages_per_split <= 0)
     pages_per_split = default_pages_per_split(batch, num_kv_heads, max_pages);
   if (pages_per_split > kMaxPagesPerSplit) return B200_ERR_INVALID_ARGUMENT;
@@ -490,7 +495,9 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
   a.out = static_cast<__nv_bfloat16*>(out);
   a.o_b = out_stride_b;
   a.o_h = out_stride_h;
-  a.ws_acc = static_cast<float*>(workspace);
+  a.ws_done = need > 0 ? static_cast<int32_t*>(workspace) : nullptr;
+  a.ws_acc = need > 0 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes)
+                      : nullptr;
   a.ws_ml = need > 0 ? a.ws_acc + static_cast<size_t>(batch) * num_heads * ms * kD : nullptr;
   a.batch = batch;
   a.num_heads = num_heads;
@@ -509,13 +516,5 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(ms));
   paged_decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(kmap, vmap, a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return B200_ERR_CUDA;
-  if (ms > 1) {
-    const int64_t warps = static_cast<int64_t>(batch) * num_heads;
-    const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
-    paged_decode_merge_kernel<<<blocks, 256, 0, s>>>(a);
-    e = cudaGetLastError();
-  }
-  return b200host::status_from_cuda(e);
+  return b200host::status_from_cuda(cudaGetLastError());
 }

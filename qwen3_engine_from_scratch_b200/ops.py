@@ -222,6 +222,32 @@ def decode_workspace_bytes(batch, num_heads, max_pages, pages_per_split=0) -> in
 
 
 _split_cache: dict[tuple[int, int, int, int], int] = {}
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_retired_workspaces: list[torch.Tensor] = []
+
+
+def _decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The decode workspace of (device, current stream), at least ``nbytes``.
+
+    Zero-filled when allocated: its split-arrival counters must start at zero,
+    and every decode launch leaves them zero, so launches on one stream (also
+    inside captured graphs) reuse it.  A grown workspace replaces the old one,
+    which is kept alive because a captured graph may still point at it.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    t = _workspaces.get(key)
+    if t is None or t.numel() < nbytes:
+        with _ws_lock:
+            t = _workspaces.get(key)
+            if t is None or t.numel() < nbytes:
+                size = max(nbytes, 2 * t.numel() if t is not None else 0)
+                if t is not None:
+                    _retired_workspaces.append(t)
+                t = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+                _workspaces[key] = t
+    return t
 
 
 def _default_split(lib, batch, num_kv_heads, max_pages) -> int:
@@ -259,7 +285,7 @@ def paged_decode(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, scale
     if pages_per_split <= 0:
         pages_per_split = _default_split(lib, B, Hkv, max_pages)
     ws_bytes = lib.b200_paged_decode_workspace_size(B, H, max_pages, pages_per_split)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    ws = _decode_workspace(q.device, ws_bytes) if ws_bytes else None
     st = lib.b200_paged_decode(
         q.data_ptr(), q.stride(0), q.stride(1),
         k_buffer.data_ptr(), v_buffer.data_ptr(),

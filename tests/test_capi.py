@@ -61,8 +61,9 @@ def test_decode_workspace_is_shape_only(native_lib):
     ws = native_lib.b200_paged_decode_workspace_size
     # one split: no workspace
     assert ws(64, 16, 16, 16) == 0
-    # 256 pages at 16 pages per split: 16 partials of (128 acc + m + l) floats per (b, h)
-    assert ws(64, 16, 256, 16) == 64 * 16 * 16 * 130 * 4
+    # 256 pages at 16 pages per split: 256 KiB of split counters, then 16 partials of
+    # (128 acc + m + l) floats per (b, h)
+    assert ws(64, 16, 256, 16) == (256 << 10) + 64 * 16 * 16 * 130 * 4
     # <= 0: an upper bound for every default split
     assert ws(64, 16, 256, 0) >= ws(64, 16, 256, native_lib.b200_paged_decode_default_split(64, 8, 256))
     assert ws(64, 16, 256, 0) == ws(64, 16, 256, 16)
