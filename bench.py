@@ -8,17 +8,20 @@ decode of Qwen3-0.6B attention -- B=64 requests, 16 q / 8 kv heads, head_dim
 128, context lengths uniform in [128, 4096], 16-token pages placed by a random
 permutation in a 32768-block pool, Q/K RMS-normed and RoPE'd at theta 1e6.
 A step is one decode step of the whole 28-layer attention stack: for every
-layer, the KV write of the new token (scatter) and the split-K decode, through
-the reference-named API ``triton_paged_attention_decode_batch``.
+layer, the KV write of the new token (scatter) and the split-K decode.  The
+step is captured once in a CUDA graph and replayed, as the reference engine
+serves decode (qwen3/graph_runner.py); ``eager_ms_per_step`` is the same step
+issued call by call from Python.
 
 ``value`` = algorithmic bytes of all ranks' steps / max-over-ranks device time
-(GB/s); inputs resident in HBM; the KV read per step (~15.5 GB) is far larger
+(GB/s); inputs resident in HBM; the KV read per step (~16 GB) is far larger
 than L2 (126 MB), so no flush is needed between steps.  ``e2e`` repeats the
-step through the same public API with the step's q/k/v copied from pinned
-host memory and the outputs copied back inside the timed region.
-``roofline`` is for the decode kernel (splits merged in-kernel by the last
-split of each request x kv head) timed live with CUDA events around every
-decode call of the timed region.
+step through the reference-named public API ``triton_paged_attention_decode_batch``
+with the step's q/k/v copied from pinned host memory and the outputs copied
+back inside the timed (graph-replayed) region; its ``eager`` field is the same
+without the graph.  ``roofline`` is for the decode kernel (splits merged
+in-kernel by the last split of each request x kv head) timed with CUDA events
+around every decode call of an eager pass over the same steps.
 
 Multi-GPU: one process per GPU (torchrun), each rank owns its own requests,
 pool and block table -- no collective on the data path ("scaling": "weak").
@@ -274,14 +277,13 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     qb.check_device_status(device)
 
+    # ---- per-call timing, eager: CUDA events around every decode call (roofline)
     ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * layers)]
     ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * layers)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(local_rank)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
     start.record(stream)
     i = 0
     for _ in range(args.steps):
@@ -295,11 +297,41 @@ def run_b200(args, rank, world, local_rank):
             i += 1
     stop.record(stream)
     torch.cuda.synchronize()
+    eager_ms = start.elapsed_time(stop)
+    decode_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / len(ev_a)
+
+    # ---- timed region: the 28-layer step captured once in a CUDA graph and
+    # replayed, as the reference's GraphRunner serves decode (qwen3/graph_runner.py)
+    def step():
+        for l in range(layers):
+            layer_call(l)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step()                              # the capture stream's workspace, allocated eagerly
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=side):
+        step()
+    for _ in range(2):
+        step_graph.replay()
+    clocks = ClockSampler(local_rank)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        step_graph.replay()
+    stop.record(stream)
+    torch.cuda.synchronize()
     clocks.stop()
     if world > 1:
         dist.barrier()
+    del step_graph
     ms = start.elapsed_time(stop)
-    decode_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / len(ev_a)
     qb.check_device_status(device)
 
     # ---- e2e: host q/k/v (pinned) -> device, the public batch API, outputs -> host
@@ -310,38 +342,75 @@ def run_b200(args, rank, world, local_rank):
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new)
     e2e_steps = max(3, min(args.steps, 50))
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        for l in range(layers):
-            o = qb.triton_paged_attention_decode_batch(dq[l], dk[l], dv[l], caches, l, scale, rows)
-            hout[l].copy_(o, non_blocking=True)
+    # layer-pipelined copies: layer l's q/k/v go up on a copy stream while
+    # earlier layers compute, each layer's output goes down on a second copy
+    # stream, and the step ends only after the last output reached the host.
+    cs_in, cs_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(layers)]
+    ev_done = [torch.cuda.Event() for _ in range(layers)]
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_step():
+        cur = torch.cuda.current_stream(device)
+        cs_in.wait_stream(cur)          # after the previous step (and joins a capture)
+        cs_out.wait_stream(cur)
+        with torch.cuda.stream(cs_in):
+            for l in range(layers):
+                dq[l].copy_(hq[l], non_blocking=True)
+                dk[l].copy_(hk[l], non_blocking=True)
+                dv[l].copy_(hv[l], non_blocking=True)
+                ev_in[l].record(cs_in)
+        for l in range(layers):
+            cur.wait_event(ev_in[l])
+            o = qb.triton_paged_attention_decode_batch(dq[l], dk[l], dv[l], caches, l, scale, rows)
+            ev_done[l].record(cur)
+            cs_out.wait_event(ev_done[l])
+            o.record_stream(cs_out)
+            with torch.cuda.stream(cs_out):
+                hout[l].copy_(o, non_blocking=True)
+        cur.wait_stream(cs_out)
+
+    def time_e2e(run):
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            run()
+        e_stop.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return e_start.elapsed_time(e_stop) / e2e_steps
+
+    # eager: every public-API call issued from Python each step
+    e2e_eager_ms = time_e2e(e2e_step)
+    # the reference engine serves decode from a CUDA graph of the whole step
+    # (qwen3/graph_runner.py): capture the same step, copies included, once
+    graph = torch.cuda.CUDAGraph()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        e2e_step()                      # warm the per-stream workspaces of the capture stream
+    stream.wait_stream(side)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(e2e_steps):
+    with torch.cuda.graph(graph, stream=side):
         e2e_step()
-    e_stop.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
-    if world > 1:
-        dist.barrier()
+    e2e_ms = time_e2e(graph.replay)
+    del graph
 
     step_bytes = layers * (decode_bytes(lens, H, Hkv) + scatter_bytes(B, Hkv))
     dec_bytes = decode_bytes(lens, H, Hkv)
-    t = torch.tensor([ms, e2e_ms, float(step_bytes), decode_ms], dtype=torch.float64, device=device)
+    t = torch.tensor([ms, e2e_ms, float(step_bytes), decode_ms, e2e_eager_ms, eager_ms],
+                     dtype=torch.float64, device=device)
     if world > 1:
         tmax = t.clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
         tsum = t.clone()
         dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
-        ms, e2e_ms = float(tmax[0]), float(tmax[1])
+        ms, e2e_ms, e2e_eager_ms, eager_ms = (float(tmax[0]), float(tmax[1]), float(tmax[4]),
+                                              float(tmax[5]))
         total_bytes_per_step = float(tsum[2])
     else:
         total_bytes_per_step = float(step_bytes)
@@ -375,12 +444,21 @@ def run_b200(args, rank, world, local_rank):
                        layers * dec_bytes / 1e9),
                    "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU"},
         "tok_per_s": round(tokens / (ms_per_step / 1e3), 1),
+        "timing": "step captured in a CUDA graph and replayed (as the reference's GraphRunner); "
+                  "eager_ms_per_step = the same step issued call by call from Python",
+        "eager_ms_per_step": round(eager_ms / args.steps, 4),
         "e2e": {"value": round(total_bytes_per_step / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4),
                 "tok_per_s": round(tokens / (e2e_ms / 1e3), 1),
                 "h2d_bytes_per_step": int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2),
                 "d2h_bytes_per_step": int(hout.numel() * 2),
-                "api": "triton_paged_attention_decode_batch (pinned host q/k/v in, host out)"},
+                "api": "triton_paged_attention_decode_batch for every layer, the step captured in "
+                       "a CUDA graph as the reference's GraphRunner serves decode; pinned host "
+                       "q/k/v in and outputs out inside the graph, per-layer copies on two copy "
+                       "streams overlapping the compute",
+                "eager": {"value": round(total_bytes_per_step / (e2e_eager_ms / 1e3) / 1e9, 1),
+                          "ms_per_step": round(e2e_eager_ms, 4),
+                          "api": "the same calls issued from Python every step"}},
         "roofline": {"kernel": "paged_decode_split_kernel",
                      "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
