@@ -540,6 +540,7 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
     sbytes = T * Hkv * D * 2 * 2 * 2 + T * 8
     peaks, src = read_peaks()
     tflops = flops / (p_ms / 1e3) / 1e12
+    prologue = bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks)
     return {"workload": w["name"], "tokens": T, "sequences": len(lens),
             "lengths": "U[64,2048]", "heads": f"{H}/{Hkv}",
             "ms_per_prefill": round(p_ms, 4), "tflops": round(tflops, 1),
@@ -551,7 +552,67 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
             "scatter": {"ms": round(s_ms, 4), "bytes": sbytes,
                         "gbs": round(sbytes / (s_ms / 1e3) / 1e9, 1),
                         "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "prologue": prologue,
             "gpu_launches_per_step": 2}
+
+
+def bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks):
+    """The fused QK-norm + RoPE + KV write over the config-3 tokens (as one request of T
+    positions, q/k/v views of a fused projection output), against the reference's
+    unfused op sequence (RMSNorm modules, apply_rotary_pos_emb, then the KV write)."""
+    qkv = torch.randn(1, T, (H + 2 * Hkv) * D, generator=g, device=device).to(torch.bfloat16)
+    q = qkv[..., :H * D].view(1, T, H, D).transpose(1, 2)
+    k = qkv[..., H * D:(H + Hkv) * D].view(1, T, Hkv, D).transpose(1, 2)
+    v = qkv[..., (H + Hkv) * D:].view(1, T, Hkv, D).transpose(1, 2)
+    wq = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(D, generator=g, device=device)).to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+    ang = torch.arange(T, device=device, dtype=torch.float32)[:, None] * inv[None]
+    emb = torch.cat([ang, ang], -1)[None]
+    cos, sin = emb.cos(), emb.sin()                      # (1, T, D) fp32 rows
+    pages = (T + 15) // 16
+    kp = torch.zeros(pages + 1, 1, Hkv, 16, D, dtype=torch.bfloat16, device=device)
+    vp = torch.zeros_like(kp)
+    bt = torch.arange(pages, dtype=torch.int32, device=device)[None].contiguous()
+    seq = torch.zeros(1, dtype=torch.int32, device=device)
+    rows = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def fused():
+        return ops.qk_norm_rope_kv_write(q, k, v, wq, wk, cos, sin, k_buffer=kp, v_buffer=vp,
+                                         seq_lens=seq, block_table_2d=bt, row_ids=rows, layer_idx=0)
+
+    def rms(x, w):   # qwen3/norm.py:22-26
+        xf = x.float()
+        return ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)) * w).to(x.dtype)
+
+    def unfused():   # qwen3/attention.py:90-95 with qwen3/rope.py:104-110, then the KV write
+        qn, kn = rms(q, wq), rms(k, wk)
+        c, s_ = cos[:, None].to(torch.bfloat16), sin[:, None].to(torch.bfloat16)
+        rq = qn * c + torch.cat([-qn[..., D // 2:], qn[..., :D // 2]], -1) * s_
+        rk = kn * c + torch.cat([-kn[..., D // 2:], kn[..., :D // 2]], -1) * s_
+        ops.kv_scatter_rows(rk, v, kp, vp, seq, bt, rows, 0)
+        return rq
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    f_ms, u_ms = timed(fused), timed(unfused)
+    nbytes = T * (H + 2 * Hkv) * D * 2 + 2 * T * D * 4 + T * H * D * 2 + 2 * T * Hkv * D * 2
+    gbs = nbytes / (f_ms / 1e3) / 1e9
+    return {"kernel": "qk_norm_rope_kv_write_kernel", "tokens": T, "ms": round(f_ms, 4),
+            "bytes": nbytes, "gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "unfused_ms": round(u_ms, 4), "speedup_vs_unfused": round(u_ms / f_ms, 2),
+            "unfused": "the reference's RMSNorm x2 + apply_rotary_pos_emb in torch ops, then "
+                       "kv_scatter_rows"}
 
 
 def read_peaks():

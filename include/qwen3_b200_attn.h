@@ -216,6 +216,42 @@ int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         float scale, int zero_pad_rows, int32_t* work_counter,
                         int32_t* dev_status, void* stream);
 
+/*
+ * Fused attention prologue: QK-RMSNorm + RoPE of q and k and the KV-cache
+ * write of the roped k and of v, one launch.  Replaces qwen3/attention.py:90-95
+ * (q_norm/k_norm, qwen3/norm.py:22-26; apply_rotary_pos_emb, qwen3/rope.py:88-110)
+ * plus the KV write that follows (update_kv_batch_triton,
+ * qwen3/kernels/paged_attention.py:292-377, or PagedKVCache.update,
+ * qwen3/PagedKVcache.py:187-214), with the reference's bf16 rounding steps:
+ *     y   = bf16((x * rsqrt(mean(x^2) + eps)) * weight)          (fp32 inside)
+ *     out = bf16(bf16(y * bf16(cos)) + bf16(rotate_half(y) * bf16(sin)))
+ * q (B, H, S, D), k and v (B, Hkv, S, D) bf16, strides (batch, head, token);
+ * q_weight/k_weight (D,) bf16; cos/sin the fp32 rows the reference's
+ * RotaryEmbedding gathered for these tokens, (B, S, D) with strides (batch,
+ * token).  q_out (B, H, S, D) receives the roped q; k_out (nullable) the roped
+ * k.  With k_pool != NULL, token s of request b is written (roped k, and v) at
+ * position seq_lens[row_ids[b]] + s of the block table, as b200_kv_scatter_rows
+ * does; k_pool == NULL skips the cache write (v may then be NULL).
+ * head_dim must be 128.  Bad rows / pages / positions set dev_status bits and
+ * skip that token's cache write.
+ */
+int b200_qk_norm_rope_kv_write(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s,
+    const void* k, int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+    const void* v, int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+    const void* q_weight, const void* k_weight, float eps,
+    const float* cos, const float* sin, int64_t cs_stride_b, int64_t cs_stride_s,
+    void* q_out, int64_t qo_stride_b, int64_t qo_stride_h, int64_t qo_stride_s,
+    void* k_out, int64_t ko_stride_b, int64_t ko_stride_h, int64_t ko_stride_s,
+    void* k_pool, void* v_pool,
+    int64_t kp_stride_blk, int64_t kp_stride_layer, int64_t kp_stride_h, int64_t kp_stride_slot,
+    int64_t vp_stride_blk, int64_t vp_stride_layer, int64_t vp_stride_h, int64_t vp_stride_slot,
+    const int32_t* seq_lens, const int32_t* block_table, int64_t bt_stride_row,
+    const int32_t* row_ids,
+    int batch, int n_tokens, int num_heads, int num_kv_heads, int head_dim, int block_size,
+    int num_blocks, int max_pages, int max_requests, int layer,
+    int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,31 @@ def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
     return (x * cos + rot * sin).astype(np.float32)
 
 
+def qk_norm_rope_bf16(x: np.ndarray, weight: np.ndarray, cos: np.ndarray, sin: np.ndarray,
+                      eps: float = 1e-6, return_terms: bool = False):
+    """QK-RMSNorm then RoPE on bf16 tensors, with the reference's rounding steps.
+
+    ``x``: (..., D) bf16 values held in float32; ``weight``: (D,) bf16 values;
+    ``cos``/``sin``: fp32 rows broadcasting against ``x`` (the RotaryEmbedding
+    gather).  Follows qwen3/norm.py:22-26 (fp32 norm, one cast to bf16) and
+    qwen3/rope.py:104-110 (cos/sin cast to bf16, then ``x*cos + rotate_half(x)*sin``
+    in bf16 arithmetic: every product and the sum rounded to bf16).  With
+    ``return_terms`` also returns the two rounded products, whose magnitude
+    bounds how far a one-ulp change of the normed input can move the output.
+    """
+    xf = np.asarray(x, dtype=np.float32)
+    ms = (xf * xf).mean(axis=-1, keepdims=True, dtype=np.float32)
+    rms = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    y = bf16_round(((xf * rms).astype(np.float32) * np.asarray(weight, np.float32)).astype(np.float32))
+    c = bf16_round(np.asarray(cos, np.float32))
+    s = bf16_round(np.asarray(sin, np.float32))
+    d = y.shape[-1]
+    rot = np.concatenate([-y[..., d // 2:], y[..., : d // 2]], axis=-1)
+    a, b = bf16_round(y * c), bf16_round(rot * s)
+    out = bf16_round(a + b)
+    return (out, a, b) if return_terms else out
+
+
 # --------------------------------------------------------------------------
 # KV-cache slot scatter
 # --------------------------------------------------------------------------

@@ -23,6 +23,7 @@ from .ops import (  # noqa: F401
     paged_decode,
     kv_scatter_rows,
     kv_scatter_slots,
+    qk_norm_rope_kv_write,
     device_status,
     clear_device_status,
     check_device_status,

@@ -1,0 +1,306 @@
+// Fused attention prologue: QK-RMSNorm + RoPE of q and k, and the KV-cache
+// write of the roped k and of v, in one launch.  Replaces, per layer,
+//   q = q_norm(q); k = k_norm(k)                      qwen3/attention.py:90-91,
+//                                                     RMSNorm qwen3/norm.py:22-26
+//   q, k = apply_rotary_pos_emb(q, k, cos, sin)       qwen3/attention.py:94-95,
+//                                                     qwen3/rope.py:88-110
+//   the KV write (update_kv_batch_triton, qwen3/kernels/paged_attention.py:292-377,
+//   or PagedKVCache.update, qwen3/PagedKVcache.py:187-214)
+// which the reference runs as separate elementwise launches.
+//
+// Rounding follows the reference's bf16 sequence exactly:
+//   RMSNorm  y = bf16((x_f32 * rsqrt(mean(x_f32^2) + eps)) * w)
+//   RoPE     c = bf16(cos), s = bf16(sin)           (.to(q.dtype), rope.py:106-107)
+//            out = bf16(bf16(y * c) + bf16(rotate_half(y) * s))
+// with rotate_half(y) = cat(-y[64:], y[:64]).  The cos/sin rows are the ones
+// the reference's RotaryEmbedding gathered (fp32, (B, S, D)).
+//
+// One warp per 8 (token, head) rows of one token, lane l holding elements
+// 4l..4l+3 of each; the RoPE partner of lane l is lane l ^ 16.  A warp issues
+// its 8 row loads and the token's cos/sin row before any math.  Rows of a
+// token: the q heads, then the k heads, then (when a pool is given) the v
+// heads.  A k row goes to k_out (optional) and to the pool slot of its
+// position; a v row only to the pool.  Pool addressing is the rows mode of the KV write: position =
+// seq_lens[row_ids[b]] + s.  Every index is range-checked; a bad one sets a
+// dev_status bit and the row's pool write is skipped.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kD = 128;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRowsPerWarp = 8;  // rows (q, k or v heads) of one token per warp
+
+struct PrologueArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t q_b, q_h, q_s, k_b, k_h, k_s, v_b, v_h, v_s;
+  const __nv_bfloat16* q_w;
+  const __nv_bfloat16* k_w;
+  float eps;
+  const float* cos;
+  const float* sin;
+  int64_t cs_b, cs_s;
+  __nv_bfloat16* q_out;
+  int64_t qo_b, qo_h, qo_s;
+  __nv_bfloat16* k_out;  // nullable
+  int64_t ko_b, ko_h, ko_s;
+  __nv_bfloat16* k_pool;  // nullable (no KV write)
+  __nv_bfloat16* v_pool;
+  int64_t kp_blk, kp_layer, kp_h, kp_slot, vp_blk, vp_layer, vp_h, vp_slot;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int64_t bt_row;
+  const int32_t* row_ids;
+  int batch, n_tokens, num_heads, num_kv_heads, block_size, num_blocks, max_pages, max_requests,
+      layer;
+  int32_t* dev_status;
+};
+
+B200_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+B200_DEVICE void load4(const __nv_bfloat16* p, float (&x)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  x[0] = b200::bf16_lo(u.x);
+  x[1] = b200::bf16_hi(u.x);
+  x[2] = b200::bf16_lo(u.y);
+  x[3] = b200::bf16_hi(u.y);
+}
+
+B200_DEVICE void store4(__nv_bfloat16* p, const float (&x)[4]) {
+  uint2 u;
+  u.x = b200::pack_bf16x2(x[0], x[1]);
+  u.y = b200::pack_bf16x2(x[2], x[3]);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// Pool slot of token (b, s): writes the element offset of (phys, layer, h=0,
+// off) into *k_off / *v_off; false (and a status bit from lane 0) if an index
+// is out of range.
+B200_DEVICE bool pool_slot(const PrologueArgs& a, int b, int s, int lane, int64_t* k_off,
+                           int64_t* v_off) {
+  const int row = a.row_ids[b];
+  if (row < 0 || row >= a.max_requests) {
+    if (lane == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_ROW);
+    return false;
+  }
+  const int64_t pos = static_cast<int64_t>(a.seq_lens[row]) + s;
+  const int64_t page = pos / a.block_size;
+  if (pos < 0 || page >= a.max_pages) {
+    if (lane == 0) b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
+    return false;
+  }
+  const int phys = a.block_table[row * a.bt_row + page];
+  if (phys < 0 || phys >= a.num_blocks) {
+    if (lane == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
+    return false;
+  }
+  const int64_t off = pos - page * a.block_size;
+  *k_off = phys * a.kp_blk + a.layer * a.kp_layer + off * a.kp_slot;
+  *v_off = phys * a.vp_blk + a.layer * a.vp_layer + off * a.vp_slot;
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int heads = a.num_heads + (a.k_pool != nullptr ? 2 : 1) * a.num_kv_heads;
+  const int chunks = (heads + kRowsPerWarp - 1) / kRowsPerWarp;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const int64_t total = static_cast<int64_t>(a.batch) * a.n_tokens * chunks;
+  if (gw >= total) return;
+  const int h0 = static_cast<int>(gw % chunks) * kRowsPerWarp;
+  const int64_t tok = gw / chunks;
+  const int s = static_cast<int>(tok % a.n_tokens);
+  const int b = static_cast<int>(tok / a.n_tokens);
+  const int d = 4 * lane;
+  const int nrows = min(kRowsPerWarp, heads - h0);
+
+  // every row load of this warp is issued before any math (memory-level parallelism)
+  uint2 raw[kRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    if (i < nrows) {
+      const int hh = h0 + i;
+      const __nv_bfloat16* src;
+      if (hh < a.num_heads) {
+        src = a.q + b * a.q_b + hh * a.q_h + s * a.q_s;
+      } else if (hh < a.num_heads + a.num_kv_heads) {
+        src = a.k + b * a.k_b + (hh - a.num_heads) * a.k_h + s * a.k_s;
+      } else {
+        src = a.v + b * a.v_b + (hh - a.num_heads - a.num_kv_heads) * a.v_h + s * a.v_s;
+      }
+      raw[i] = *reinterpret_cast<const uint2*>(src + d);
+    }
+  }
+  const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d);
+  const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d);
+  const float cf[4] = {bf16_round(c4.x), bf16_round(c4.y), bf16_round(c4.z), bf16_round(c4.w)};
+  const float sf[4] = {bf16_round(s4.x), bf16_round(s4.y), bf16_round(s4.z), bf16_round(s4.w)};
+
+  int64_t k_off = 0, v_off = 0;
+  const bool kv_rows = h0 + nrows > a.num_heads;
+  const bool write_pool =
+      kv_rows && a.k_pool != nullptr && pool_slot(a, b, s, lane, &k_off, &v_off);
+
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    if (i >= nrows) break;
+    const int hh = h0 + i;
+    const bool is_q = hh < a.num_heads;
+    const bool is_k = !is_q && hh < a.num_heads + a.num_kv_heads;
+    if (!is_q && !is_k) {  // v row: a plain copy into the pool
+      if (write_pool)
+        *reinterpret_cast<uint2*>(a.v_pool + v_off +
+                                  (hh - a.num_heads - a.num_kv_heads) * a.vp_h + d) = raw[i];
+      continue;
+    }
+    const float x[4] = {b200::bf16_lo(raw[i].x), b200::bf16_hi(raw[i].x), b200::bf16_lo(raw[i].y),
+                        b200::bf16_hi(raw[i].y)};
+    // RMSNorm in fp32: mean of squares over the 128 elements of the row
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rms = __frsqrt_rn(ss / static_cast<float>(kD) + a.eps);
+    float w[4];
+    load4((is_q ? a.q_w : a.k_w) + d, w);
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[e] = bf16_round((x[e] * rms) * w[e]);
+    // RoPE: partner elements d +- 64 live in lane ^ 16
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float p = __shfl_xor_sync(0xffffffffu, y[e], 16);
+      const float rot = lane < 16 ? -p : p;
+      r[e] = bf16_round(bf16_round(y[e] * cf[e]) + bf16_round(rot * sf[e]));
+    }
+    if (is_q) {
+      store4(a.q_out + b * a.qo_b + hh * a.qo_h + s * a.qo_s + d, r);
+    } else {
+      const int h = hh - a.num_heads;
+      if (a.k_out != nullptr) store4(a.k_out + b * a.ko_b + h * a.ko_h + s * a.ko_s + d, r);
+      if (write_pool) store4(a.k_pool + k_off + h * a.kp_h + d, r);
+    }
+  }
+}
+
+bool mult8(int64_t s) { return (s & 7) == 0; }
+
+}  // namespace
+
+extern "C" int b200_qk_norm_rope_kv_write(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s, const void* k,
+    int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s, const void* v,
+    int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s, const void* q_weight,
+    const void* k_weight, float eps, const float* cos, const float* sin, int64_t cs_stride_b,
+    int64_t cs_stride_s, void* q_out, int64_t qo_stride_b, int64_t qo_stride_h,
+    int64_t qo_stride_s, void* k_out, int64_t ko_stride_b, int64_t ko_stride_h,
+    int64_t ko_stride_s, void* k_pool, void* v_pool, int64_t kp_stride_blk,
+    int64_t kp_stride_layer, int64_t kp_stride_h, int64_t kp_stride_slot, int64_t vp_stride_blk,
+    int64_t vp_stride_layer, int64_t vp_stride_h, int64_t vp_stride_slot,
+    const int32_t* seq_lens, const int32_t* block_table, int64_t bt_stride_row,
+    const int32_t* row_ids, int batch, int n_tokens, int num_heads, int num_kv_heads,
+    int head_dim, int block_size, int num_blocks, int max_pages, int max_requests, int layer,
+    int32_t* dev_status, void* stream) {
+  if (batch < 0 || n_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || n_tokens == 0) return B200_OK;
+  if (head_dim != kD) return B200_ERR_UNSUPPORTED;
+  if (!q || !k || !q_weight || !k_weight || !cos || !sin || !q_out)
+    return B200_ERR_INVALID_ARGUMENT;
+  const bool pool = k_pool != nullptr;
+  if (pool) {
+    if (!v || !v_pool || !seq_lens || !block_table || !row_ids || block_size <= 0 ||
+        num_blocks <= 0 || max_pages <= 0 || max_requests <= 0 || bt_stride_row <= 0 ||
+        layer < 0)
+      return B200_ERR_INVALID_ARGUMENT;
+  }
+  // 8-byte row pieces for the bf16 rows, 16-byte pieces for the fp32 cos/sin rows
+  const void* ptrs8[] = {q, k, q_weight, k_weight, q_out};
+  for (const void* p : ptrs8)
+    if ((reinterpret_cast<uintptr_t>(p) & 7) != 0) return B200_ERR_ALIGNMENT;
+  if (!b200host::aligned16(cos) || !b200host::aligned16(sin)) return B200_ERR_ALIGNMENT;
+  if ((cs_stride_b & 3) != 0 || (cs_stride_s & 3) != 0) return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h,
+                             k_stride_s, qo_stride_b, qo_stride_h, qo_stride_s};
+  for (int64_t st : strides)
+    if ((st & 3) != 0) return B200_ERR_ALIGNMENT;
+  if (k_out != nullptr) {
+    if ((reinterpret_cast<uintptr_t>(k_out) & 7) != 0 || (ko_stride_b & 3) != 0 ||
+        (ko_stride_h & 3) != 0 || (ko_stride_s & 3) != 0)
+      return B200_ERR_ALIGNMENT;
+  }
+  if (pool) {
+    if ((reinterpret_cast<uintptr_t>(v) & 7) != 0 || !b200host::aligned16(k_pool) ||
+        !b200host::aligned16(v_pool))
+      return B200_ERR_ALIGNMENT;
+    const int64_t ps[] = {v_stride_b, v_stride_h, v_stride_s, kp_stride_blk, kp_stride_layer,
+                          kp_stride_h, kp_stride_slot, vp_stride_blk, vp_stride_layer,
+                          vp_stride_h, vp_stride_slot};
+    for (int64_t st : ps)
+      if ((st & 3) != 0) return B200_ERR_ALIGNMENT;
+  }
+  const int heads = num_heads + (pool ? 2 : 1) * num_kv_heads;
+  const int64_t warps =
+      static_cast<int64_t>(batch) * n_tokens * ((heads + kRowsPerWarp - 1) / kRowsPerWarp);
+  const int64_t blocks = (warps + kWarps - 1) / kWarps;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+
+  PrologueArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.q_b = q_stride_b;
+  a.q_h = q_stride_h;
+  a.q_s = q_stride_s;
+  a.k_b = k_stride_b;
+  a.k_h = k_stride_h;
+  a.k_s = k_stride_s;
+  a.v_b = v_stride_b;
+  a.v_h = v_stride_h;
+  a.v_s = v_stride_s;
+  a.q_w = static_cast<const __nv_bfloat16*>(q_weight);
+  a.k_w = static_cast<const __nv_bfloat16*>(k_weight);
+  a.eps = eps;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_b = cs_stride_b;
+  a.cs_s = cs_stride_s;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.qo_b = qo_stride_b;
+  a.qo_h = qo_stride_h;
+  a.qo_s = qo_stride_s;
+  a.k_out = static_cast<__nv_bfloat16*>(k_out);
+  a.ko_b = ko_stride_b;
+  a.ko_h = ko_stride_h;
+  a.ko_s = ko_stride_s;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.kp_blk = kp_stride_blk;
+  a.kp_layer = kp_stride_layer;
+  a.kp_h = kp_stride_h;
+  a.kp_slot = kp_stride_slot;
+  a.vp_blk = vp_stride_blk;
+  a.vp_layer = vp_stride_layer;
+  a.vp_h = vp_stride_h;
+  a.vp_slot = vp_stride_slot;
+  a.seq_lens = seq_lens;
+  a.block_table = block_table;
+  a.bt_row = bt_stride_row;
+  a.row_ids = row_ids;
+  a.batch = batch;
+  a.n_tokens = n_tokens;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.block_size = block_size;
+  a.num_blocks = num_blocks;
+  a.max_pages = max_pages;
+  a.max_requests = max_requests;
+  a.layer = layer;
+  a.dev_status = dev_status;
+  qk_norm_rope_kv_write_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(a);
+  return b200host::status_from_cuda(cudaGetLastError());
+}

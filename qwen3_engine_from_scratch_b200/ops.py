@@ -45,6 +45,7 @@ __all__ = [
     "paged_decode",
     "kv_scatter_rows",
     "kv_scatter_slots",
+    "qk_norm_rope_kv_write",
     "device_status",
     "clear_device_status",
     "check_device_status",
@@ -182,6 +183,71 @@ def update_kv_batch_triton(k_new, v_new, k_buffer, v_buffer, seq_lens, block_tab
     """
     kv_scatter_rows(k_new.unsqueeze(2), v_new.unsqueeze(2), k_buffer, v_buffer, seq_lens,
                     block_table_2d, row_ids, layer_idx)
+
+
+def qk_norm_rope_kv_write(q, k, v, q_weight, k_weight, cos, sin, eps=1e-6, k_buffer=None,
+                          v_buffer=None, seq_lens=None, block_table_2d=None, row_ids=None,
+                          layer_idx=0, return_k=False):
+    """Fused QK-RMSNorm + RoPE + KV-cache write (one launch).
+
+    Replaces ``q_norm``/``k_norm`` and ``apply_rotary_pos_emb`` of
+    qwen3/attention.py:90-95 and the KV write that follows it, with the
+    reference's bf16 rounding steps (qwen3/norm.py:22-26, qwen3/rope.py:104-110).
+    q: (B, H, S, D), k/v: (B, Hkv, S, D) bf16 views (e.g. of the fused qkv
+    projection); q_weight/k_weight: (D,) bf16; cos/sin: the (B, S, D) fp32 rows of
+    the reference's RotaryEmbedding for these tokens.  With the pool arguments
+    given, token s of request b lands at position ``seq_lens[row_ids[b]] + s``
+    (as ``kv_scatter_rows``).  Returns ``q_out`` (B, H, S, D), and the roped k
+    as well when ``return_k``.
+    """
+    assert q.dim() == 4 and k.dim() == 4, "q/k must be (B, heads, S, D)"
+    for name, t in (("q", q), ("k", k), ("q_weight", q_weight), ("k_weight", k_weight)):
+        assert t.dtype == torch.bfloat16 and t.is_cuda, f"{name} must be bf16 on the GPU"
+    assert cos.dtype == torch.float32 and sin.dtype == torch.float32, "cos/sin must be fp32"
+    B, H, S, D = q.shape
+    Hkv = k.shape[1]
+    assert k.shape == (B, Hkv, S, D) and D == HEAD_DIM, "k shape / head_dim mismatch"
+    assert cos.shape == (B, S, D) and sin.shape == cos.shape, "cos/sin must be (B, S, D)"
+    assert cos.stride() == sin.stride(), "cos/sin must share strides"
+    q = q if q.stride(-1) == 1 else q.contiguous()
+    k = k if k.stride(-1) == 1 else k.contiguous()
+    cos = cos if cos.stride(-1) == 1 else cos.contiguous()
+    sin = sin if sin.stride() == cos.stride() else sin.contiguous()
+    q_weight = q_weight.contiguous()
+    k_weight = k_weight.contiguous()
+    q_out = torch.empty((B, H, S, D), dtype=torch.bfloat16, device=q.device)
+    k_out = torch.empty((B, Hkv, S, D), dtype=torch.bfloat16, device=q.device) if return_k else None
+    pool = k_buffer is not None
+    if pool:
+        assert v is not None and v.shape == k.shape and v.dtype == torch.bfloat16
+        _check_pool(k_buffer, v_buffer)
+        _check_table(block_table_2d, seq_lens, row_ids)
+        assert k_buffer.dim() == 5 and k_buffer.shape[2] == Hkv and k_buffer.shape[4] == D, \
+            "pool must be (num_blocks, num_layers, Hkv, block_size, D)"
+        assert row_ids.numel() == B, "row_ids must have one entry per request"
+        v = v if v.stride(-1) == 1 else v.contiguous()
+    lib = _native.load()
+    nul = (None, 0, 0, 0)
+    kb = k_buffer if pool else None
+    vb = v_buffer if pool else None
+    st = lib.b200_qk_norm_rope_kv_write(
+        q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+        k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+        *((v.data_ptr(), v.stride(0), v.stride(1), v.stride(2)) if pool else nul),
+        q_weight.data_ptr(), k_weight.data_ptr(), float(eps),
+        cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.stride(1),
+        q_out.data_ptr(), q_out.stride(0), q_out.stride(1), q_out.stride(2),
+        *((k_out.data_ptr(), k_out.stride(0), k_out.stride(1), k_out.stride(2)) if return_k else nul),
+        kb.data_ptr() if pool else None, vb.data_ptr() if pool else None,
+        *((kb.stride(0), kb.stride(1), kb.stride(2), kb.stride(3)) if pool else (0, 0, 0, 0)),
+        *((vb.stride(0), vb.stride(1), vb.stride(2), vb.stride(3)) if pool else (0, 0, 0, 0)),
+        seq_lens.data_ptr() if pool else None, block_table_2d.data_ptr() if pool else None,
+        block_table_2d.stride(0) if pool else 0, row_ids.data_ptr() if pool else None,
+        B, S, H, Hkv, D, kb.shape[3] if pool else BLOCK_SIZE, kb.shape[0] if pool else 0,
+        block_table_2d.shape[1] if pool else 0, block_table_2d.shape[0] if pool else 0,
+        int(layer_idx), _status_ptr(q.device), _stream())
+    _native.check(st, "b200_qk_norm_rope_kv_write")
+    return (q_out, k_out) if return_k else q_out
 
 
 def kv_scatter_slots(k, v, k_buffer, v_buffer, slot_mapping, layer_idx=0):

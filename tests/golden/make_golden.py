@@ -253,10 +253,46 @@ def make_norm_rope(ref):
     print("norm_rope: ok")
 
 
+def make_norm_rope_bf16(ref):
+    """The reference's QK-norm + RoPE modules on bf16 tensors (its serving dtype)."""
+    torch = ref["torch"]
+    RMSNorm, RotaryEmbedding, apply_rope = ref["RMSNorm"], ref["RotaryEmbedding"], ref["apply_rope"]
+    B, H, Hkv, S, D = 3, 4, 2, 5, 128
+    q = synth.det_normal(811, (B, H, S, D)).astype(np.float32) * 2.0
+    k = synth.det_normal(812, (B, Hkv, S, D)).astype(np.float32)
+    wq = 1.0 + 0.1 * synth.det_normal(813, (D,)).astype(np.float32)
+    wk = 1.0 + 0.1 * synth.det_normal(814, (D,)).astype(np.float32)
+    seq = np.array([0, 37, 250], dtype=np.int64)          # positions start per request
+    pos = seq[:, None] + np.arange(S)[None]                 # (B, S)
+    bf = torch.bfloat16
+    qn_mod, kn_mod = RMSNorm(D, 1e-6), RMSNorm(D, 1e-6)
+    with torch.no_grad():
+        qn_mod.weight.copy_(torch.from_numpy(wq))
+        kn_mod.weight.copy_(torch.from_numpy(wk))
+        qn_mod, kn_mod = qn_mod.to(bf), kn_mod.to(bf)
+        rope = RotaryEmbedding(D, 1e6, max_seq_len=512)
+        qb = torch.from_numpy(q).to(bf)
+        kb = torch.from_numpy(k).to(bf)
+        cos, sin = rope(torch.from_numpy(pos))
+        qr, kr = apply_rope(qn_mod(qb), kn_mod(kb), cos, sin)
+    as_bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    meta = dict(case="norm_rope_bf16", seeds=[811, 812, 813, 814], D=D, theta=1e6, eps=1e-6,
+                B=B, H=H, Hkv=Hkv, S=S, seq_lens=seq.tolist(),
+                reference_fn="qwen3/norm.py:RMSNorm (bf16 weight), qwen3/rope.py:"
+                             "RotaryEmbedding/apply_rotary_pos_emb on bf16 q/k")
+    np.savez_compressed(os.path.join(HERE, "norm_rope_bf16.npz"), meta=np.array(json.dumps(meta)),
+                        q_bits=as_bits(qb), k_bits=as_bits(kb),
+                        wq_bits=as_bits(qn_mod.weight.data), wk_bits=as_bits(kn_mod.weight.data),
+                        cos=cos.numpy(), sin=sin.numpy(),
+                        q_rope_bits=as_bits(qr), k_rope_bits=as_bits(kr))
+    print("norm_rope_bf16: ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("QWEN3_REFERENCE"),
                     help="path of the reference repository checkout")
+    ap.add_argument("--only", default=None, help="generate only this fixture (e.g. norm_rope_bf16)")
     args = ap.parse_args()
     if not args.reference or not os.path.isdir(args.reference):
         sys.exit("make_golden.py: pass --reference <path> (the reference checkout)")
@@ -273,11 +309,17 @@ def main():
                paged_attention=paged_attention, Qwen3Attention=Qwen3Attention,
                Qwen3Config=Qwen3Config, RMSNorm=RMSNorm, RotaryEmbedding=RotaryEmbedding,
                apply_rope=apply_rotary_pos_emb)
+    want = (lambda name: args.only is None or args.only == name)
     for name, cfg in DECODE_CASES.items():
-        make_decode_case(name, cfg, ref)
+        if want(name):
+            make_decode_case(name, cfg, ref)
     for name, cfg in PREFILL_CASES.items():
-        make_prefill_case(name, cfg, ref)
-    make_norm_rope(ref)
+        if want(name):
+            make_prefill_case(name, cfg, ref)
+    if want("norm_rope"):
+        make_norm_rope(ref)
+    if want("norm_rope_bf16"):
+        make_norm_rope_bf16(ref)
 
 
 if __name__ == "__main__":

@@ -170,6 +170,24 @@ def test_oracle_norm_rope_matches_reference():
     assert np.abs(kr - case["k_rope"]).max() < 1e-5
 
 
+def test_oracle_norm_rope_bf16_bitexact_vs_reference():
+    """bf16 QK-norm + RoPE (the serving dtype): the oracle's rounding sequence
+    reproduces the reference modules bit for bit, and the stored bf16 inputs
+    are the seeded values rounded once."""
+    case = gc.load("norm_rope_bf16")
+    m = case["meta"]
+    f = oa.from_bf16_bits
+    q, k = f(case["q_bits"]), f(case["k_bits"])
+    assert np.array_equal(case["q_bits"],
+                          oa.bf16_bits(synth.det_normal(m["seeds"][0], q.shape) * np.float32(2.0)))
+    assert np.array_equal(case["k_bits"], oa.bf16_bits(synth.det_normal(m["seeds"][1], k.shape)))
+    cos, sin = case["cos"][:, None], case["sin"][:, None]
+    qo = oa.qk_norm_rope_bf16(q, f(case["wq_bits"]), cos, sin, m["eps"])
+    ko = oa.qk_norm_rope_bf16(k, f(case["wk_bits"]), cos, sin, m["eps"])
+    assert np.array_equal(oa.bf16_bits(qo), case["q_rope_bits"])
+    assert np.array_equal(oa.bf16_bits(ko), case["k_rope_bits"])
+
+
 def test_roofline_numerators():
     lens = np.array([128, 4096])
     b = oa.decode_bytes(lens, 16, 8)
