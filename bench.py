@@ -541,6 +541,7 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
     peaks, src = read_peaks()
     tflops = flops / (p_ms / 1e3) / 1e12
     prologue = bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks)
+    chunked = bench_paged_prefill(torch, ops, device, rank, H, Hkv, D, steps, warmup, peaks)
     return {"workload": w["name"], "tokens": T, "sequences": len(lens),
             "lengths": "U[64,2048]", "heads": f"{H}/{Hkv}",
             "ms_per_prefill": round(p_ms, 4), "tflops": round(tflops, 1),
@@ -553,7 +554,59 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
                         "gbs": round(sbytes / (s_ms / 1e3) / 1e9, 1),
                         "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
             "prologue": prologue,
+            "paged_prefill": chunked,
             "gpu_launches_per_step": 2}
+
+
+def bench_paged_prefill(torch, ops, device, rank, H, Hkv, D, steps, warmup, peaks):
+    """Chunked prefill over the paged cache: 32 sequences with U[0, 2048] tokens
+    already cached and a new chunk of U[64, 512] tokens each (pages placed by a
+    random permutation), attention of the new tokens over context + chunk."""
+    rng = np.random.default_rng(5000 + rank)
+    ctx = rng.integers(0, 2048, size=32, endpoint=True)
+    new = rng.integers(64, 512, size=32, endpoint=True)
+    g = torch.Generator(device=device).manual_seed(91 + rank)
+    totals = ctx + new
+    max_pages = int(((totals + 15) // 16).max())
+    nb = int(((totals + 15) // 16).sum()) + 8
+    kp = torch.randn(nb, Hkv, 16, D, generator=g, device=device).to(torch.bfloat16)
+    vp = torch.randn(nb, Hkv, 16, D, generator=g, device=device).to(torch.bfloat16)
+    perm = torch.randperm(nb, generator=g, device=device).to(torch.int32)
+    bt = torch.full((32, max_pages), -1, dtype=torch.int32, device=device)
+    used = 0
+    for i in range(32):
+        npg = int((totals[i] + 15) // 16)
+        bt[i, :npg] = perm[used:used + npg]
+        used += npg
+    seq = torch.from_numpy(ctx.astype(np.int32)).to(device)
+    rows = torch.arange(32, dtype=torch.int32, device=device)
+    T = int(new.sum())
+    q = torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(new)]).astype(np.int32)).to(device)
+    out = torch.empty(T, H, D, dtype=torch.bfloat16, device=device)
+    mx = int(new.max())
+
+    def call():
+        ops.paged_prefill(q, kp, vp, bt, seq, rows, cu, D ** -0.5, max_new_tokens=mx, out=out)
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    # causal pairs: new token t of sequence i sees ctx_i + t + 1 keys
+    pairs = int(sum(int(n) * int(c) + int(n) * (int(n) + 1) // 2 for c, n in zip(ctx, new)))
+    flops = 4 * H * D * pairs
+    tf = flops / (ms / 1e3) / 1e12
+    return {"kernel": "varlen_prefill_kernel (paged mode)", "sequences": 32,
+            "cached": "U[0,2048]", "new_tokens": T, "chunk": "U[64,512]", "ms": round(ms, 4),
+            "flops_per_launch": flops, "tflops": round(tf, 1),
+            "frac_bf16": round(tf / peaks["bf16_tflops"], 4)}
 
 
 def bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks):

@@ -217,6 +217,34 @@ int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         int32_t* dev_status, void* stream);
 
 /*
+ * Chunked prefill over the paged KV cache (prefix continuation).  No
+ * counterpart in the reference: its prefill ignores cached context
+ * (qwen3/attention.py:109-120; chunked prefill and prefix caching are open
+ * items of its ENGINE_COMPARISON.md).  Sequence i has ctx_i =
+ * seq_lens[row_ids[i]] tokens cached and len_i = cu_seqlens[i+1] -
+ * cu_seqlens[i] new tokens, rows [cu_seqlens[i], cu_seqlens[i+1]) of q/out;
+ * the new tokens' K/V must already be in the pool at positions ctx_i ..
+ * ctx_i + len_i - 1 (b200_kv_scatter_rows / b200_qk_norm_rope_kv_write write
+ * there).  New token t attends causally to keys 0 .. ctx_i + t, all read from
+ * the pool pages block_table[row, p] (the layout of b200_paged_decode:
+ * k_pool/v_pool the layer's first element, strides (block, head, slot));
+ * decode is the len_i == 1 case.  q (T, H, D), out (T, H, D): strides (token,
+ * head).  max_new_tokens >= every len_i.  work_counter as in
+ * b200_varlen_prefill.  Bad rows / table entries set dev_status bits.
+ */
+int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                       const void* k_pool, const void* v_pool,
+                       int64_t kv_stride_blk, int64_t kv_stride_h, int64_t kv_stride_slot,
+                       const int32_t* block_table, int64_t bt_stride_row,
+                       const int32_t* seq_lens, const int32_t* row_ids,
+                       const int32_t* cu_seqlens, void* out,
+                       int64_t o_stride_t, int64_t o_stride_h,
+                       int num_seqs, int total_tokens, int max_new_tokens,
+                       int num_heads, int num_kv_heads, int head_dim, int block_size,
+                       int num_blocks, int max_pages, int max_requests, float scale,
+                       int32_t* work_counter, int32_t* dev_status, void* stream);
+
+/*
  * Fused attention prologue: QK-RMSNorm + RoPE of q and k and the KV-cache
  * write of the roped k and of v, one launch.  Replaces qwen3/attention.py:90-95
  * (q_norm/k_norm, qwen3/norm.py:22-26; apply_rotary_pos_emb, qwen3/rope.py:88-110)

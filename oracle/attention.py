@@ -260,6 +260,41 @@ def varlen_prefill(q, k, v, cu_seqlens, scale):
     return out
 
 
+def paged_prefill(q, k_pool, v_pool, block_table_2d, ctx_lens, row_ids, cu_seqlens, scale):
+    """Chunked prefill over a paged cache (the prefix-continuation case the
+    reference leaves open, qwen3/attention.py:109-120): the causal softmax of
+    qwen3/attention.py:193-207 with the new tokens' positions offset by the
+    cached context.  q (T, H, D); k_pool/v_pool one layer (num_blocks, Hkv, 16,
+    D); sequence i = pool row row_ids[i] with ctx_lens[i] cached tokens and
+    its new tokens at rows cu[i]..cu[i+1] of q, their K/V already in the pool.
+    Returns (T, H, D) float32.
+    """
+    q = np.asarray(q, np.float32)
+    T, H, D = q.shape
+    Hkv = k_pool.shape[1]
+    G = H // Hkv
+    out = np.zeros((T, H, D), np.float32)
+    for i in range(len(cu_seqlens) - 1):
+        s0, s1 = int(cu_seqlens[i]), int(cu_seqlens[i + 1])
+        n, c, row = s1 - s0, int(ctx_lens[i]), int(row_ids[i])
+        if n == 0:
+            continue
+        total = c + n
+        pages = block_table_2d[row, :(total + 15) // 16]
+        k = np.asarray(k_pool[pages], np.float32).transpose(0, 2, 1, 3).reshape(-1, Hkv, D)[:total]
+        v = np.asarray(v_pool[pages], np.float32).transpose(0, 2, 1, 3).reshape(-1, Hkv, D)[:total]
+        kq = np.repeat(k, G, axis=1)                         # (total, H, D)
+        vq = np.repeat(v, G, axis=1)
+        sc = np.einsum("thd,jhd->htj", q[s0:s1], kq) * np.float32(scale)
+        mask = np.arange(total)[None, :] <= (c + np.arange(n))[:, None]
+        sc = np.where(mask[None], sc, -np.inf)
+        sc = sc - sc.max(-1, keepdims=True)
+        p = np.exp(sc)
+        p /= p.sum(-1, keepdims=True)
+        out[s0:s1] = np.einsum("htj,jhd->thd", p, vq)
+    return out
+
+
 def prefill_batched(q, k, v, lens, scaling):
     """Right-padded batch adapter (qwen3/kernels/flash_attention_varlen.py:197-258).
 

@@ -67,6 +67,9 @@ SIGNATURES = {
     "b200_varlen_prefill": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                  _P, _I64, _I64, _P, _P, _I, _I, _I, _I, _I, _I,
                                  _F, _I, _P, _P, _P]),
+    "b200_paged_prefill": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P,
+                                _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                _F, _P, _P, _P]),
     "b200_qk_norm_rope_kv_write": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64,
                                         _P, _I64, _I64, _I64, _P, _P, _F, _P, _P, _I64, _I64,
                                         _P, _I64, _I64, _I64, _P, _I64, _I64, _I64,

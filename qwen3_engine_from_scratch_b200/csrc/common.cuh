@@ -118,6 +118,16 @@ B200_DEVICE void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
       : "memory");
 }
 
+// 4-D tiled tensor load without a cache hint (no multicast), completing on `bar`.
+B200_DEVICE void tma_load_4d_nohint(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0,
+                                    int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // 3-D tiled tensor load (no multicast), completing on `bar`.
 B200_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                              int c2) {

@@ -97,6 +97,15 @@ struct PrefillArgs {
   float scale_log2;
   int32_t* dev_status;
   int32_t* sched;       // nullable: [0] next item, [1] CTAs done (zero at launch, reset at exit)
+  // paged mode (chunked prefill): the new tokens of sequence i sit at positions
+  // ctx_i .. ctx_i + len_i - 1 after ctx_i = seq_lens[row_ids[i]] cached ones;
+  // every key (cached and new) is read from the paged pool
+  int paged;
+  const int32_t* row_ids;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int64_t bt_row;
+  int num_blocks, max_pages, max_requests;
 };
 
 // Work list shared by every CTA (each CTA builds the same one in shared
@@ -109,7 +118,10 @@ struct PrefillArgs {
 struct WorkList {
   int len[kMaxSeqs];
   int start[kMaxSeqs];
-  uint32_t key[kMaxSeqs];        // sorted: (kMaxTiles - 1 - tiles) << 16 | sequence
+  int ctx[kMaxSeqs];             // cached positions before the new tokens (paged mode)
+  int row[kMaxSeqs];             // pool row (paged mode)
+  int qtiles[kMaxSeqs];          // 128-row query tiles of the new tokens
+  uint32_t key[kMaxSeqs];        // sorted: (kMaxTiles - 1 - key tiles) << 16 | sequence
   int seq_prefix[kMaxSeqs + 1];  // items before the r-th sequence of the sorted order
   int pad_prefix[kMaxSeqs + 1];  // padded adapter: zero rows before sequence s (all heads)
   unsigned char pad_ok[kMaxSeqs];  // rows [len, max_seqlen) of sequence s lie inside the output
@@ -119,6 +131,7 @@ struct WorkList {
 
 struct Item {
   int start, len, hk, n_kv;
+  int ctx, row;     // paged mode: cached positions, pool row
   int h[2], m0[2];  // query head and first row of tile 0 / tile 1
 };
 
@@ -141,12 +154,13 @@ B200_DEVICE Item decode_item(const PrefillArgs& a, const WorkList& W, int k) {
   const int rem = k - W.seq_prefix[lo];
   const int step = rem / per;
   const int p = rem - step * per;
-  const uint32_t key = W.key[lo];
-  const int seq = static_cast<int>(key & 0xFFFFu);
-  const int tiles = kMaxTiles - 1 - static_cast<int>(key >> 16);
+  const int seq = static_cast<int>(W.key[lo] & 0xFFFFu);
+  const int tiles = W.qtiles[seq];
   Item it;
   it.start = W.start[seq];
   it.len = W.len[seq];
+  it.ctx = W.ctx[seq];
+  it.row = W.row[seq];
   if (a.pair_heads) {
     it.h[0] = 2 * p;
     it.h[1] = 2 * p + 1;
@@ -157,7 +171,8 @@ B200_DEVICE Item decode_item(const PrefillArgs& a, const WorkList& W, int k) {
     it.m0[1] = it.m0[0] + kBM;  // may lie past the sequence: computed, never stored
   }
   it.hk = it.h[0] / a.group;
-  it.n_kv = (min(it.len, it.m0[1] + kBM) + kBN - 1) / kBN;  // causal: keys < m0 + 128
+  // causal: keys < ctx + m0 + 128
+  it.n_kv = (it.ctx + min(it.len, it.m0[1] + kBM) + kBN - 1) / kBN;
   return it;
 }
 
@@ -299,6 +314,33 @@ B200_DEVICE bool wait_or_flag(uint32_t bar, uint32_t parity, Barriers* B, int32_
   return false;
 }
 
+// Paged mode: key tile j (keys [128j, 128j + 128)) of an item from the pool,
+// 8 pages x two 64-column boxes of [16 slots][64 d] (2 KB each, stacked in the
+// canonical [128 keys][64 d] block).  Pages past the sequence repeat its last
+// page, so masked keys read finite data; a bad table entry is flagged and
+// replaced by block 0.
+B200_DEVICE void load_kv_tile_paged(const PrefillArgs& a, const Item& it, const CUtensorMap* map,
+                                    uint32_t dst, uint32_t bar, int j) {
+  const int last_page = (it.ctx + it.len - 1) / 16;
+  const int32_t* bt = a.block_table + static_cast<int64_t>(it.row) * a.bt_row;
+  int phys[kBN / 16];
+#pragma unroll
+  for (int i = 0; i < kBN / 16; ++i) {
+    const int pg = min(j * (kBN / 16) + i, last_page);
+    int ph = bt[pg];
+    if (ph < 0 || ph >= a.num_blocks) {
+      b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
+      ph = 0;
+    }
+    phys[i] = ph;
+  }
+#pragma unroll
+  for (int i = 0; i < kBN / 16; ++i) {
+    b200::tma_load_4d_nohint(dst + i * 2048, map, bar, 0, 0, it.hk, phys[i]);
+    b200::tma_load_4d_nohint(dst + kKVBlock + i * 2048, map, bar, 64, 0, it.hk, phys[i]);
+  }
+}
+
 // Build the work list (every CTA computes the same one).  All threads call.
 B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
   const int n = a.num_seqs;
@@ -309,17 +351,36 @@ B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
       const int start = a.cu[s];
       int len = a.lens != nullptr ? a.lens[s] : a.cu[s + 1] - start;
       const int rows = a.zero_pad ? a.max_seqlen : len;  // rows this sequence writes
-      const bool bad = len < 0 || len > a.max_seqlen || start < 0 ||
-                       static_cast<int64_t>(start) + rows > a.total_tokens;
+      bool bad = len < 0 || len > a.max_seqlen || start < 0 ||
+                 static_cast<int64_t>(start) + rows > a.total_tokens;
+      int ctx = 0, row = 0;
+      if (a.paged && !bad) {
+        row = a.row_ids[s];
+        if (row < 0 || row >= a.max_requests) {
+          b200::flag_error(a.dev_status, B200_DEV_BAD_ROW);
+          len = 0;
+        } else {
+          ctx = a.seq_lens[row];
+          if (ctx < 0 || static_cast<int64_t>(ctx) + len > static_cast<int64_t>(a.max_pages) * 16 ||
+              static_cast<int64_t>(ctx) + len > static_cast<int64_t>(kMaxTiles - 1) * kBN)
+            bad = true;
+        }
+      }
       if (bad) {
         b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
         len = 0;
+        ctx = 0;
       }
       W.start[s] = start;
       W.len[s] = len;
+      W.ctx[s] = ctx;
+      W.row[s] = row;
       W.pad_ok[s] = bad ? 0 : 1;
       const int nt = (len + kBM - 1) / kBM;
-      W.key[s] = (static_cast<uint32_t>(kMaxTiles - 1 - nt) << 16) | static_cast<uint32_t>(s);
+      W.qtiles[s] = nt;
+      // heaviest first: by the key tiles of the sequence's last query tile
+      const int kt = len > 0 ? (ctx + len + kBN - 1) / kBN : 0;
+      W.key[s] = (static_cast<uint32_t>(kMaxTiles - 1 - kt) << 16) | static_cast<uint32_t>(s);
     } else {
       W.key[s] = 0xFFFFFFFFu;
     }
@@ -346,7 +407,7 @@ B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
     int acc = 0;
     for (int r = 0; r < n; ++r) {
       W.seq_prefix[r] = acc;
-      acc += seq_steps(a, kMaxTiles - 1 - static_cast<int>(W.key[r] >> 16)) * per;
+      acc += seq_steps(a, W.qtiles[W.key[r] & 0xFFFFu]) * per;
     }
     W.seq_prefix[n] = acc;
     W.n_items = acc;
@@ -477,8 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           const uint32_t dk = sK + s * kKVBytes;
           b200::mbar_arrive_expect_tx(bar_k(s), kKVBytes);
-          b200::tma_load_3d(dk, &tmk, bar_k(s), 0, it.hk, it.start + j * kBN);
-          b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, it.hk, it.start + j * kBN);
+          if (a.paged) {
+            load_kv_tile_paged(a, it, &tmk, dk, bar_k(s), j);
+          } else {
+            b200::tma_load_3d(dk, &tmk, bar_k(s), 0, it.hk, it.start + j * kBN);
+            b200::tma_load_3d(dk + kKVBlock, &tmk, bar_k(s), 64, it.hk, it.start + j * kBN);
+          }
         }
       }
     } else if (lane == 1) {
@@ -496,8 +561,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           const uint32_t dv = sV + s * kKVBytes;
           b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
-          b200::tma_load_3d(dv, &tmv, bar_v(s), 0, it.hk, it.start + j * kBN);
-          b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, it.hk, it.start + j * kBN);
+          if (a.paged) {
+            load_kv_tile_paged(a, it, &tmv, dv, bar_v(s), j);
+          } else {
+            b200::tma_load_3d(dv, &tmv, bar_v(s), 0, it.hk, it.start + j * kBN);
+            b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, it.hk, it.start + j * kBN);
+          }
         }
       }
     }
@@ -618,9 +687,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld(xs + c * 32);
         float* x = reinterpret_cast<float*>(xs);
 
+        // key positions: cached ones first (paged mode), then the new tokens
         const int n0 = j * kBN;
-        if (n0 + kBN - 1 > qpos || n0 + kBN > it.len) {
-          const int lim = min(qpos + 1, it.len) - n0;  // keys [n0, n0 + lim) are visible
+        const int qabs = it.ctx + qpos, kend = it.ctx + it.len;
+        if (n0 + kBN - 1 > qabs || n0 + kBN > kend) {
+          const int lim = min(qabs + 1, kend) - n0;  // keys [n0, n0 + lim) are visible
 #pragma unroll
           for (int c = 0; c < kBN; ++c)
             if (c >= lim) x[c] = -INFINITY;
@@ -798,6 +869,55 @@ int encode_rows_map(CUtensorMap* map, const void* base, int heads, int tokens, i
              : B200_ERR_TENSOR_MAP;
 }
 
+// Launches the kernel over `num_seqs` sequences, at most kMaxSeqs per launch;
+// `base` carries every field but the per-launch sequence slices.
+int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   PrefillArgs base, const int32_t* cu_seqlens, const int32_t* lens_opt,
+                   const int32_t* row_ids, int num_seqs, void* stream) {
+  int st = ensure_smem_attr(b200host::current_device());
+  if (st != B200_OK) return st;
+  const int sms = b200host::sm_count(b200host::current_device());
+  if (sms <= 0) return B200_ERR_CUDA;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const int pairs = exp_fma_pairs();
+  for (int s0 = 0; s0 < num_seqs; s0 += kMaxSeqs) {
+    PrefillArgs a = base;
+    a.cu = cu_seqlens + s0;
+    a.lens = lens_opt != nullptr ? lens_opt + s0 : nullptr;
+    a.row_ids = row_ids != nullptr ? row_ids + s0 : nullptr;
+    a.num_seqs = num_seqs - s0 < kMaxSeqs ? num_seqs - s0 : kMaxSeqs;
+    dim3 grid(static_cast<unsigned>(sms));  // one persistent CTA per SM
+    switch (pairs) {
+      case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+    }
+    st = b200host::status_from_cuda(cudaGetLastError());
+    if (st != B200_OK) return st;
+  }
+  return B200_OK;
+}
+
+PrefillArgs base_args(void* out, int64_t o_stride_t, int64_t o_stride_h, int num_heads,
+                      int num_kv_heads, int max_seqlen, int total_tokens, float scale,
+                      int32_t* work_counter, int32_t* dev_status) {
+  PrefillArgs a{};
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_t = o_stride_t;
+  a.o_h = o_stride_h;
+  a.num_heads = num_heads;
+  a.group = num_heads / num_kv_heads;
+  a.max_seqlen = max_seqlen;
+  a.total_tokens = total_tokens;
+  a.pair_heads = (a.group % 2) == 0 ? 1 : 0;
+  a.scale_log2 = scale * kLog2e;
+  a.dev_status = dev_status;
+  a.sched = work_counter;
+  return a;
+}
+
 }  // namespace
 
 extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
@@ -834,41 +954,76 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
     st = encode_rows_map(&tv, v, num_kv_heads, total_tokens, v_stride_t, v_stride_h, kBN);
   if (st != B200_OK) return st;
 
-  st = ensure_smem_attr(b200host::current_device());
-  if (st != B200_OK) return st;
-  const int sms = b200host::sm_count(b200host::current_device());
-  if (sms <= 0) return B200_ERR_CUDA;
-  cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  const int pairs = exp_fma_pairs();
+  PrefillArgs a = base_args(out, o_stride_t, o_stride_h, num_heads, num_kv_heads, max_seqlen,
+                            total_tokens, scale, work_counter, dev_status);
+  a.zero_pad = zero_pad_rows != 0;
+  return launch_prefill(tq, tk, tv, a, cu_seqlens, seq_lens_opt, nullptr, num_seqs, stream);
+}
 
-  // sequences are independent: launch at most kMaxSeqs of them at a time
-  for (int s0 = 0; s0 < num_seqs; s0 += kMaxSeqs) {
-    PrefillArgs a;
-    a.cu = cu_seqlens + s0;
-    a.lens = seq_lens_opt != nullptr ? seq_lens_opt + s0 : nullptr;
-    a.out = static_cast<__nv_bfloat16*>(out);
-    a.o_t = o_stride_t;
-    a.o_h = o_stride_h;
-    a.num_seqs = num_seqs - s0 < kMaxSeqs ? num_seqs - s0 : kMaxSeqs;
-    a.num_heads = num_heads;
-    a.group = num_heads / num_kv_heads;
-    a.max_seqlen = max_seqlen;
-    a.zero_pad = zero_pad_rows != 0;
-    a.total_tokens = total_tokens;
-    a.pair_heads = (a.group % 2) == 0 ? 1 : 0;
-    a.scale_log2 = scale * kLog2e;
-    a.dev_status = dev_status;
-    a.sched = work_counter;
-    dim3 grid(static_cast<unsigned>(sms));  // one persistent CTA per SM
-    switch (pairs) {
-      case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-    }
-    st = b200host::status_from_cuda(cudaGetLastError());
-    if (st != B200_OK) return st;
+extern "C" int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                                  const void* k_pool, const void* v_pool, int64_t kv_stride_blk,
+                                  int64_t kv_stride_h, int64_t kv_stride_slot,
+                                  const int32_t* block_table, int64_t bt_stride_row,
+                                  const int32_t* seq_lens, const int32_t* row_ids,
+                                  const int32_t* cu_seqlens, void* out, int64_t o_stride_t,
+                                  int64_t o_stride_h, int num_seqs, int total_tokens,
+                                  int max_new_tokens, int num_heads, int num_kv_heads,
+                                  int head_dim, int block_size, int num_blocks, int max_pages,
+                                  int max_requests, float scale, int32_t* work_counter,
+                                  int32_t* dev_status, void* stream) {
+  if (num_seqs < 0 || total_tokens < 0 || max_new_tokens < 0 || num_heads <= 0 ||
+      num_kv_heads <= 0 || num_blocks <= 0 || max_pages <= 0 || max_requests <= 0 ||
+      bt_stride_row <= 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0 || total_tokens == 0 || max_new_tokens == 0) return B200_OK;
+  if (!q || !k_pool || !v_pool || !block_table || !seq_lens || !row_ids || !cu_seqlens || !out)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != kD || block_size != 16) return B200_ERR_UNSUPPORTED;
+  if (num_heads % num_kv_heads != 0) return B200_ERR_INVALID_ARGUMENT;
+  const int n_tiles = (max_new_tokens + kBM - 1) / kBM;
+  if (n_tiles > kMaxTiles) return B200_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(n_tiles) * kMaxSeqs * num_heads > 0x7fffffff)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (!b200host::aligned16(q) || !b200host::aligned16(out) || !b200host::aligned16(k_pool) ||
+      !b200host::aligned16(v_pool))
+    return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {q_stride_t, q_stride_h, o_stride_t, o_stride_h,
+                             kv_stride_blk, kv_stride_h, kv_stride_slot};
+  for (int64_t s : strides)
+    if (!mult8(s)) return B200_ERR_ALIGNMENT;
+
+  CUtensorMap tq, tk, tv;
+  int st = encode_rows_map(&tq, q, num_heads, total_tokens, q_stride_t, q_stride_h, kBM);
+  if (st != B200_OK) return st;
+  {
+    // one layer of the pool: (d = 128, slot = 16, kv head, block), boxes of one page
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), 16u,
+                                static_cast<cuuint64_t>(num_kv_heads),
+                                static_cast<cuuint64_t>(num_blocks)};
+    const cuuint64_t strides_b[3] = {static_cast<cuuint64_t>(kv_stride_slot) * 2,
+                                     static_cast<cuuint64_t>(kv_stride_h) * 2,
+                                     static_cast<cuuint64_t>(kv_stride_blk) * 2};
+    const cuuint32_t box[4] = {64, 16, 1, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (b200host::encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                               const_cast<void*>(k_pool), dims, strides_b, box, es,
+                               CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS ||
+        b200host::encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                               const_cast<void*>(v_pool), dims, strides_b, box, es,
+                               CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS)
+      return B200_ERR_TENSOR_MAP;
   }
-  return B200_OK;
+
+  PrefillArgs a = base_args(out, o_stride_t, o_stride_h, num_heads, num_kv_heads,
+                            max_new_tokens, total_tokens, scale, work_counter, dev_status);
+  a.paged = 1;
+  a.seq_lens = seq_lens;
+  a.block_table = block_table;
+  a.bt_row = bt_stride_row;
+  a.num_blocks = num_blocks;
+  a.max_pages = max_pages;
+  a.max_requests = max_requests;
+  return launch_prefill(tq, tk, tv, a, cu_seqlens, nullptr, row_ids, num_seqs, stream);
 }

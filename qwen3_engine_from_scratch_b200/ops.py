@@ -46,6 +46,7 @@ __all__ = [
     "kv_scatter_rows",
     "kv_scatter_slots",
     "qk_norm_rope_kv_write",
+    "paged_prefill",
     "device_status",
     "clear_device_status",
     "check_device_status",
@@ -512,6 +513,50 @@ def flash_attention_prefill(q, k, v, cu_seqlens, scale, num_heads, num_kv_heads,
     out = torch.empty((q.shape[0], num_heads, head_dim), dtype=q.dtype, device=q.device)
     _prefill(q, k, v, out, cu_seqlens.contiguous(), None, max_seqlen, scale, num_heads,
              num_kv_heads, head_dim, False)
+    return out
+
+
+def paged_prefill(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, cu_seqlens, scale,
+                  max_new_tokens=None, out=None):
+    """Chunked prefill over the paged KV cache (no reference counterpart: its
+    prefill ignores cached context, qwen3/attention.py:109-120).
+
+    q: (T, H, D) bf16, the packed new tokens of every sequence (cu_seqlens);
+    k_buffer/v_buffer: (num_blocks, Hkv, 16, D) layer views of the pool, which
+    already holds the new tokens' K/V at positions seq_lens[row] .. +len-1
+    (e.g. written by ``qk_norm_rope_kv_write``).  Sequence i = pool row
+    row_ids[i]; new token t attends to positions 0 .. seq_lens[row] + t.
+    ``max_new_tokens`` (keyword) avoids reading the lengths back to the host.
+    Returns (T, H, D) bf16.
+    """
+    assert q.dim() == 3 and q.dtype == torch.bfloat16, "q must be (T, H, D) bf16"
+    assert k_buffer.dim() == 4, "k_buffer must be a (num_blocks, Hkv, block_size, D) layer view"
+    _check_pool(k_buffer, v_buffer)
+    _check_table(block_table_2d, seq_lens, row_ids)
+    assert cu_seqlens.dtype == torch.int32 and cu_seqlens.is_cuda, "cu_seqlens must be int32 on GPU"
+    T, H, D = q.shape
+    nb, Hkv, bs, d_p = k_buffer.shape
+    assert d_p == D and k_buffer.stride() == v_buffer.stride(), "pool views mismatch"
+    n = cu_seqlens.numel() - 1
+    assert row_ids.numel() == n, "row_ids must have one entry per sequence"
+    if max_new_tokens is None:
+        cu = cu_seqlens.cpu()
+        max_new_tokens = int((cu[1:] - cu[:-1]).max().item()) if n > 0 else 0
+    q = _vec_ready(q, 0, 1)
+    if out is None:
+        out = torch.empty((T, H, D), dtype=torch.bfloat16, device=q.device)
+    lib = _native.load()
+    st = lib.b200_paged_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_buffer.data_ptr(), v_buffer.data_ptr(),
+        k_buffer.stride(0), k_buffer.stride(1), k_buffer.stride(2),
+        block_table_2d.data_ptr(), block_table_2d.stride(0),
+        seq_lens.data_ptr(), row_ids.data_ptr(), cu_seqlens.contiguous().data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        n, T, int(max_new_tokens), H, Hkv, D, bs, nb, block_table_2d.shape[1],
+        block_table_2d.shape[0], float(scale), _work_counter(q.device).data_ptr(),
+        _status_ptr(q.device), _stream())
+    _native.check(st, "b200_paged_prefill")
     return out
 
 

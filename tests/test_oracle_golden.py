@@ -193,3 +193,39 @@ def test_roofline_numerators():
     b = oa.decode_bytes(lens, 16, 8)
     assert b == (128 + 4096) * 8 * 128 * 2 * 2 + 2 * 16 * 128 * 4 + (8 + 256) * 4 + 16
     assert oa.prefill_flops([1, 2], 16) == 4 * 16 * 128 * (1 + 3)
+
+
+def test_oracle_paged_prefill_restates_the_reference_prefill():
+    """Chunked prefill has no reference counterpart; its oracle is pinned through
+    the reference-pinned varlen oracle: with no cached context it equals it, and
+    a sequence prefilled in two chunks equals the rows of one full prefill."""
+    case = gc.load(gc.case_names("prefill")[0])
+    m = case["meta"]
+    inp = gc.prefill_inputs(case)
+    lens = m["lens"]
+    q, k, v = (gc.pack_varlen(inp[n], lens) for n in ("q", "k", "v"))
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    Hkv, D = m["Hkv"], 128
+    nb = sum((L + 15) // 16 for L in lens) + 4
+    kp = np.zeros((nb, Hkv, 16, D), np.float32)
+    vp = np.zeros_like(kp)
+    perm = np.random.default_rng(5).permutation(nb)
+    bt = np.full((len(lens), 64), -1, np.int32)
+    used = 0
+    for i, L in enumerate(lens):
+        npg = (L + 15) // 16
+        bt[i, :npg] = perm[used:used + npg]
+        used += npg
+        t = np.arange(L)
+        kp[bt[i, t // 16], :, t % 16] = k[cu[i] + t]
+        vp[bt[i, t // 16], :, t % 16] = v[cu[i] + t]
+    rows = np.arange(len(lens))
+    full = oa.varlen_prefill(q, k, v, cu, m["scaling"])
+    assert np.abs(oa.paged_prefill(q, kp, vp, bt, np.zeros(len(lens)), rows, cu, m["scaling"])
+                  - full).max() < 1e-5
+    # the longest sequence in two chunks: a third cached, the rest new
+    i = int(np.argmax(lens))
+    c = lens[i] // 3
+    s0, s1 = cu[i] + c, cu[i + 1]
+    part = oa.paged_prefill(q[s0:s1], kp, vp, bt, [c], [i], np.array([0, s1 - s0]), m["scaling"])
+    assert np.abs(part - full[s0:s1]).max() < 1e-5
