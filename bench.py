@@ -474,9 +474,64 @@ def run_b200(args, rank, world, local_rank):
             line["prefill"] = run_prefill(args, rank, world, local_rank, steps=10, warmup=3)
         except RuntimeError as e:   # the prefill kernel is optional for the decode headline
             line["prefill"] = {"error": str(e)[:200]}
+    if not args.no_prefill:
+        try:
+            line["sampling"] = bench_sampling(device)
+        except RuntimeError as e:
+            line["sampling"] = {"error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_budget)
     return line
+
+
+def bench_sampling(device, steps=20, warmup=3):
+    """Fused sampler on a Qwen3 decode batch (64 x 151936 bf16 logits) against
+    torch.topk alone, the first of the reference path's two launches
+    (qwen3/sampling.py:215-216), and greedy against torch.argmax."""
+    import torch
+    from qwen3_engine_from_scratch_b200 import ops
+    g = torch.Generator(device=device).manual_seed(17)
+    B, V = 64, 151936
+    logits = (torch.randn(B, V, generator=g, device=device) * 3).to(torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps * 1e3   # us
+
+    def graphed(fn):   # device time of one call: the call captured in a CUDA graph
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            fn()
+        t = timed(graph.replay)
+        del graph
+        return t
+
+    calls = {"fused": lambda: ops.sample_tokens(logits, 0.7, 50, 0.9, seed=1),
+             "torch_topk_only": lambda: torch.topk(logits, 50, dim=-1, largest=True, sorted=True),
+             "greedy": lambda: ops.sample_tokens(logits, 0.0),
+             "torch_argmax": lambda: logits.argmax(dim=-1)}
+    res = {"kernel": "sample_chunk_kernel + sample_row_kernel", "batch": B, "vocab": V,
+           "dtype": "bf16", "params": "temperature 0.7, top_k 50, top_p 0.9",
+           "timing": "per call from Python (eager, host included) and device time of the "
+                     "call replayed from a CUDA graph"}
+    for name, fn in calls.items():
+        res[name + "_us"] = round(timed(fn), 2)
+        res[name + "_graph_us"] = round(graphed(fn), 2)
+    return res
 
 
 def run_prefill(args, rank, world, local_rank, steps, warmup):

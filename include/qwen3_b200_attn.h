@@ -48,6 +48,7 @@ typedef enum {
 #define B200_DEV_BAD_SLOT 0x4     /* slot_mapping entry past the pool           */
 #define B200_DEV_SEQ_OVERFLOW 0x8 /* position needs a page past max_pages       */
 #define B200_DEV_TIMEOUT 0x10     /* a bounded pipeline wait gave up            */
+#define B200_DEV_BAD_PARAM 0x20   /* a per-row parameter outside its range      */
 
 /* Human-readable text for a b200_status value. */
 const char* b200_status_string(int status);
@@ -215,6 +216,35 @@ int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                         int num_heads, int num_kv_heads, int head_dim,
                         float scale, int zero_pad_rows, int32_t* work_counter,
                         int32_t* dev_status, void* stream);
+
+/*
+ * Fused token sampling.  Replaces the reference's sample_tokens Triton path:
+ * the batched torch.topk (qwen3/sampling.py:215-216) and _sample_topk_kernel
+ * (qwen3/sampling.py:112-178), plus its greedy argmax (:253-254), in one launch.
+ * logits (batch, vocab) fp32 (logits_bf16 = 0) or bf16, row stride in elements;
+ * temperature / top_k / top_p: per-row device arrays, each nullable: NULL
+ * gives every row the matching *_all value.  Per row:
+ *   temperature <= 0: argmax (first index of the maximum);
+ *   1 <= top_k <= 1024: the k largest logits (ties by ascending index),
+ *     x = logit / temperature, softmax, keep rank 0 and every rank whose
+ *     preceding probability mass is <= top_p, Gumbel-max with the uniform
+ *     of Triton's tl.rand(seed, row * block_k + rank) (Philox4x32-10), as the
+ *     reference kernel does (block_k = max(16, next power of two of the
+ *     batch's largest top_k) reproduces its random stream);
+ *   top_k == 0 and top_p >= 1: Gumbel-max over the whole row (uniforms at
+ *     row * vocab + index).
+ * Other top_k values are clamped to 1024 and flagged B200_DEV_BAD_PARAM.
+ * Two launches: chunks of 8192 logits select their candidates into
+ * `workspace` (b200_sample_workspace_size(batch, vocab, block_k) bytes,
+ * 16-byte aligned, no initialisation needed), then one CTA per row merges
+ * them and samples.  vocab <= 262144.  out: (batch,) int64 token ids.
+ */
+size_t b200_sample_workspace_size(int batch, int vocab, int block_k);
+int b200_sample_tokens(const void* logits, int logits_bf16, int64_t stride_row, int batch,
+                       int vocab, const float* temperature, const int32_t* top_k,
+                       const float* top_p, float temperature_all, int top_k_all,
+                       float top_p_all, uint64_t seed, int block_k, void* workspace,
+                       size_t workspace_bytes, int64_t* out, int32_t* dev_status, void* stream);
 
 /*
  * Chunked prefill over the paged KV cache (prefix continuation).  No

@@ -25,6 +25,7 @@ from .ops import (  # noqa: F401
     kv_scatter_slots,
     qk_norm_rope_kv_write,
     paged_prefill,
+    sample_tokens,
     device_status,
     clear_device_status,
     check_device_status,

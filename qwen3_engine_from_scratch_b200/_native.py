@@ -27,6 +27,7 @@ DEV_BAD_PAGE = 0x2
 DEV_BAD_SLOT = 0x4
 DEV_SEQ_OVERFLOW = 0x8
 DEV_TIMEOUT = 0x10
+DEV_BAD_PARAM = 0x20
 
 DEV_STATUS_NAMES = {
     DEV_BAD_ROW: "row id outside the block table",
@@ -34,6 +35,7 @@ DEV_STATUS_NAMES = {
     DEV_BAD_SLOT: "slot_mapping entry outside the pool",
     DEV_SEQ_OVERFLOW: "sequence position past the block table",
     DEV_TIMEOUT: "pipeline wait timed out",
+    DEV_BAD_PARAM: "per-row parameter outside its range (clamped)",
 }
 
 # Every symbol include/qwen3_b200_attn.h declares, with its ctypes signature.
@@ -67,6 +69,9 @@ SIGNATURES = {
     "b200_varlen_prefill": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
                                  _P, _I64, _I64, _P, _P, _I, _I, _I, _I, _I, _I,
                                  _F, _I, _P, _P, _P]),
+    "b200_sample_workspace_size": (_SZ, [_I, _I, _I]),
+    "b200_sample_tokens": (_I, [_P, _I, _I64, _I, _I, _P, _P, _P, _F, _I, _F, ctypes.c_uint64,
+                                _I, _P, _SZ, _P, _P, _P]),
     "b200_paged_prefill": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P, _P,
                                 _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I,
                                 _F, _P, _P, _P]),

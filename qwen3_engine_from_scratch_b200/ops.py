@@ -47,6 +47,7 @@ __all__ = [
     "kv_scatter_slots",
     "qk_norm_rope_kv_write",
     "paged_prefill",
+    "sample_tokens",
     "device_status",
     "clear_device_status",
     "check_device_status",
@@ -514,6 +515,111 @@ def flash_attention_prefill(q, k, v, cu_seqlens, scale, num_heads, num_kv_heads,
     _prefill(q, k, v, out, cu_seqlens.contiguous(), None, max_seqlen, scale, num_heads,
              num_kv_heads, head_dim, False)
     return out
+
+
+_scratch_lock = threading.Lock()
+_scratches: dict[tuple[str, int, int], torch.Tensor] = {}
+
+
+def _scratch(device: torch.device, name: str, nbytes: int) -> torch.Tensor:
+    """A reusable uninitialised buffer of (name, device, current stream), at
+    least ``nbytes`` (kept alive once handed out: a captured graph may use it)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (name, idx, torch.cuda.current_stream(idx).cuda_stream)
+    t = _scratches.get(key)
+    if t is None or t.numel() < nbytes:
+        with _scratch_lock:
+            t = _scratches.get(key)
+            if t is None or t.numel() < nbytes:
+                if t is not None:
+                    _retired_workspaces.append(t)
+                t = torch.empty(max(nbytes, 16), dtype=torch.uint8,
+                                device=torch.device("cuda", idx))
+                _scratches[key] = t
+    return t
+
+
+_SEED_COUNTER = 0
+
+
+def _next_seed() -> int:
+    """Per-call seed when none is given (qwen3/sampling.py:42-48)."""
+    global _SEED_COUNTER
+    _SEED_COUNTER += 1
+    return (torch.initial_seed() + _SEED_COUNTER * 0x9E3779B1) & 0x7FFFFFFF
+
+
+def _row_param(value, B, device, dtype):
+    if isinstance(value, torch.Tensor):
+        t = value.to(device=device, dtype=dtype)
+        return t.expand(B).contiguous() if t.ndim == 0 else t.contiguous()
+    if isinstance(value, (list, tuple)):
+        return torch.tensor(value, device=device, dtype=dtype)
+    return torch.full((B,), value, device=device, dtype=dtype)
+
+
+def _host_list(value, B):
+    if isinstance(value, torch.Tensor):
+        return None if value.is_cuda else value.reshape(-1).tolist() * (B if value.ndim == 0 else 1)
+    if isinstance(value, (list, tuple)):
+        return list(value)
+    return [value] * B
+
+
+def sample_tokens(logits, temperature=0.0, top_k=0, top_p=1.0, seed=None):
+    """Fused sampling of (B, V) logits -> (B, 1) int64 token ids, one launch
+    (qwen3/sampling.py:234-270: the torch.topk + _sample_topk_kernel path, and
+    the greedy argmax).  Parameters: scalars or per-row lists / tensors.
+
+    temperature <= 0: argmax.  1 <= top_k <= 1024: top-k, top-p and Gumbel-max
+    with the reference kernel's random stream for the same ``seed``.
+    top_k == 0 with top_p == 1: temperature sampling over the whole vocabulary
+    (the reference uses torch.multinomial there: same distribution, another
+    stream).  top_k == 0 with top_p < 1 (a nucleus over the whole sorted
+    vocabulary) is not supported and raises ValueError.
+    """
+    if logits.ndim != 2:
+        raise ValueError(f"logits must be (B, V), got shape={tuple(logits.shape)}")
+    assert logits.is_cuda and logits.dtype in (torch.float32, torch.bfloat16), \
+        "logits must be fp32 or bf16 on the GPU"
+    B, V = logits.shape
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    dev = logits.device
+    temps, ks, ps = _host_list(temperature, B), _host_list(top_k, B), _host_list(top_p, B)
+    if ks is not None and ps is not None and temps is not None:
+        for t, k, p in zip(temps, ks, ps):
+            if float(t) > 0 and int(k) == 0 and float(p) < 1.0:
+                raise ValueError("top_k == 0 with top_p < 1 is not supported by the fused sampler")
+            if float(t) > 0 and not (0 <= int(k) <= 1024):
+                raise ValueError("top_k must be in [0, 1024]")
+        sampled_k = [min(int(k), V) for t, k in zip(temps, ks) if float(t) > 0 and int(k) > 0]
+        max_k = max(sampled_k) if sampled_k else 1
+        block_k = max(16, 1 << (max_k - 1).bit_length())
+    else:
+        block_k = 1024        # device parameters: the largest k the kernel takes
+    # a parameter shared by every row goes to the kernel as a scalar (no device array)
+    scalar = lambda v: not isinstance(v, (torch.Tensor, list, tuple))
+    t_t = None if scalar(temperature) else _row_param(temperature, B, dev, torch.float32)
+    k_t = None if scalar(top_k) else _row_param(top_k, B, dev, torch.int32)
+    p_t = None if scalar(top_p) else _row_param(top_p, B, dev, torch.float32)
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    if seed is None:
+        seed = _next_seed()
+    lib = _native.load()
+    ws_bytes = int(lib.b200_sample_workspace_size(B, V, int(block_k)))
+    ws = _scratch(dev, "sample", ws_bytes)
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    st = lib.b200_sample_tokens(logits.data_ptr(), int(logits.dtype == torch.bfloat16),
+                                logits.stride(0), B, V, ptr(t_t), ptr(k_t), ptr(p_t),
+                                float(temperature) if t_t is None else 0.0,
+                                int(top_k) if k_t is None else 0,
+                                float(top_p) if p_t is None else 1.0,
+                                int(seed) & 0xFFFFFFFFFFFFFFFF, int(block_k),
+                                ws.data_ptr(), ws_bytes, out.data_ptr(), _status_ptr(dev),
+                                _stream())
+    _native.check(st, "b200_sample_tokens")
+    return out.unsqueeze(1)
 
 
 def paged_prefill(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, cu_seqlens, scale,

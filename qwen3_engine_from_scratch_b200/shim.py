@@ -38,6 +38,10 @@ _BINDINGS = {
     ("qwen3.kernels.paged_attention", "update_kv_batch_triton"): ops.update_kv_batch_triton,
     ("qwen3.kernels.flash_attention_varlen", "flash_attention_prefill"): ops.flash_attention_prefill,
     ("qwen3.kernels.flash_attention_varlen", "flash_attention_prefill_batched"): ops.flash_attention_prefill_batched,
+    # fused sampler (qwen3/sampling.py:234-270); callers that did `from qwen3.sampling
+    # import sample_tokens` before install() keep the reference's function
+    ("qwen3.sampling", "sample_tokens"): ops.sample_tokens,
+    ("qwen3", "sample_tokens"): ops.sample_tokens,
 }
 
 _saved: dict = {}

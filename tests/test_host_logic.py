@@ -92,7 +92,8 @@ def test_shim_binds_into_reference_modules(monkeypatch):
         assert attn.triton_paged_attention_decode is ops.triton_paged_attention_decode
         assert attn.flash_attention_prefill_batched is ops.flash_attention_prefill_batched
         assert kvc.update_kv_batch_triton is ops.update_kv_batch_triton
-        assert len(bound) == 10
+        assert len(bound) == 12
+        assert importlib.import_module("qwen3.sampling").sample_tokens is ops.sample_tokens
     finally:
         shim.uninstall()
     attn = importlib.import_module("qwen3.attention")

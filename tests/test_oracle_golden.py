@@ -229,3 +229,20 @@ def test_oracle_paged_prefill_restates_the_reference_prefill():
     s0, s1 = cu[i] + c, cu[i + 1]
     part = oa.paged_prefill(q[s0:s1], kp, vp, bt, [c], [i], np.array([0, s1 - s0]), m["scaling"])
     assert np.abs(part - full[s0:s1]).max() < 1e-5
+
+
+def test_oracle_sampling_bitexact_vs_reference_kernel():
+    """Philox4x32-10 words and uniforms equal Triton's tl.randint / tl.rand, and
+    the oracle's tokens equal the reference's _sample_topk_kernel on every row
+    (fixture made under Triton's CPU interpreter)."""
+    from oracle import sampling as osmp
+    case = gc.load("sampling")
+    m = case["meta"]
+    for i, sd in enumerate(m["rand_seeds"]):
+        n = case["rand_bits"].shape[1]
+        assert np.array_equal(osmp.philox4x32_10(sd, np.arange(n))[0], case["rand_bits"][i])
+        assert np.array_equal(osmp.rand_uniform(sd, np.arange(n)), case["rand_u"][i])
+    logits = synth.det_normal(m["seed_logits"], (m["B"], m["V"])) * np.float32(m["scale"])
+    tok = osmp.sample_tokens(logits, m["temperature"], m["top_k"], m["top_p"], m["seed"],
+                             m["block_k"])
+    assert np.array_equal(tok, case["tokens"])
