@@ -247,6 +247,13 @@ B200_DEVICE uint64_t ex2_fma2(uint64_t y) {
                  __int_as_float(__float_as_int(t1) * 8388608 + __float_as_int(p1)));
 }
 
+// 32-byte global store (sm_100 256-bit access); p must be 32-byte aligned.
+B200_DEVICE void st_global_v8(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]),
+               "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 B200_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 B200_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

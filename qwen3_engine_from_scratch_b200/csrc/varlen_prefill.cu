@@ -94,6 +94,7 @@ struct PrefillArgs {
   int64_t o_t, o_h;
   int num_seqs, num_heads, group, max_seqlen, zero_pad, total_tokens;
   int pair_heads;       // 1: an item is query heads 2p, 2p+1 (group even); 0: two row tiles
+  int out32;            // out rows 32-byte aligned (base and strides): 256-bit stores
   float scale_log2;
   int32_t* dev_status;
   int32_t* sched;       // nullable: [0] next item, [1] CTAs done (zero at launch, reset at exit)
@@ -785,14 +786,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
                               static_cast<int64_t>(it.h[t]) * a.o_h;
+        if (a.out32) {
+          // 32-byte stores: every row piece is a full sector
 #pragma unroll
-        for (int e = 0; e < kD; e += 8) {
-          uint4 v;
-          v.x = b200::pack_bf16x2(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv);
-          v.y = b200::pack_bf16x2(__uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
-          v.z = b200::pack_bf16x2(__uint_as_float(ov[e + 4]) * inv, __uint_as_float(ov[e + 5]) * inv);
-          v.w = b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv, __uint_as_float(ov[e + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + e) = v;
+          for (int e = 0; e < kD; e += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              w[i] = b200::pack_bf16x2(__uint_as_float(ov[e + 2 * i]) * inv,
+                                       __uint_as_float(ov[e + 2 * i + 1]) * inv);
+            b200::st_global_v8(orow + e, w);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < kD; e += 8) {
+            uint4 v;
+            v.x = b200::pack_bf16x2(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv);
+            v.y = b200::pack_bf16x2(__uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
+            v.z = b200::pack_bf16x2(__uint_as_float(ov[e + 4]) * inv, __uint_as_float(ov[e + 5]) * inv);
+            v.w = b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv, __uint_as_float(ov[e + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + e) = v;
+          }
         }
       }
     }
@@ -912,6 +926,8 @@ PrefillArgs base_args(void* out, int64_t o_stride_t, int64_t o_stride_h, int num
   a.max_seqlen = max_seqlen;
   a.total_tokens = total_tokens;
   a.pair_heads = (a.group % 2) == 0 ? 1 : 0;
+  a.out32 = (reinterpret_cast<uintptr_t>(out) & 31) == 0 && (o_stride_t & 15) == 0 &&
+            (o_stride_h & 15) == 0;
   a.scale_log2 = scale * kLog2e;
   a.dev_status = dev_status;
   a.sched = work_counter;
