@@ -12,8 +12,8 @@ environment switches read on every call:
   qwen3/PagedKVcache.py.
 
 ``install()`` rebinds those module-level names to the B200 implementations, so
-the reference's own switches route to them and ``GraphRunner`` captures them
-unchanged.  Setting ``QWEN3_FLASH_ATTN=b200`` before importing this module
+the reference's own switches route to them and the reference's ``GraphRunner``
+(or this package's, bound in its place) captures them unchanged.  Setting ``QWEN3_FLASH_ATTN=b200`` before importing this module
 installs it automatically.  ``QWEN3_PAGED_ATTN`` must stay ``triton`` (its
 default): the reference compares it with ``==`` and any other value silently
 routes decode to its PyTorch fallback.  ``uninstall()`` restores the originals.
@@ -24,7 +24,7 @@ from __future__ import annotations
 import importlib
 import os
 
-from . import ops
+from . import graph_runner, ops
 
 # (module, attribute) -> replacement
 _BINDINGS = {
@@ -42,6 +42,9 @@ _BINDINGS = {
     # import sample_tokens` before install() keep the reference's function
     ("qwen3.sampling", "sample_tokens"): ops.sample_tokens,
     ("qwen3", "sample_tokens"): ops.sample_tokens,
+    # decode-step graph pool (qwen3/graph_runner.py:26-200), same constructor and replay;
+    # as above, only callers that import the name after install() get it
+    ("qwen3.graph_runner", "GraphRunner"): graph_runner.GraphRunner,
 }
 
 _saved: dict = {}

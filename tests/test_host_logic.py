@@ -92,8 +92,10 @@ def test_shim_binds_into_reference_modules(monkeypatch):
         assert attn.triton_paged_attention_decode is ops.triton_paged_attention_decode
         assert attn.flash_attention_prefill_batched is ops.flash_attention_prefill_batched
         assert kvc.update_kv_batch_triton is ops.update_kv_batch_triton
-        assert len(bound) == 12
+        assert len(bound) == 13
         assert importlib.import_module("qwen3.sampling").sample_tokens is ops.sample_tokens
+        from qwen3_engine_from_scratch_b200 import graph_runner
+        assert importlib.import_module("qwen3.graph_runner").GraphRunner is graph_runner.GraphRunner
     finally:
         shim.uninstall()
     attn = importlib.import_module("qwen3.attention")
@@ -122,6 +124,20 @@ def test_reference_signatures_match():
         assert got[:len(params)] == params, (name, got)
 
 
+def test_graph_runner_signature_matches_reference(monkeypatch):
+    """GraphRunner takes the reference's constructor and replay arguments."""
+    import inspect
+    monkeypatch.syspath_prepend(REFERENCE)
+    import importlib
+    ref = importlib.import_module("qwen3.graph_runner").GraphRunner
+    from qwen3_engine_from_scratch_b200 import shim
+    ours = shim._BINDINGS[("qwen3.graph_runner", "GraphRunner")]
+    for meth in ("__init__", "replay", "free"):
+        want = list(inspect.signature(getattr(ref, meth)).parameters)
+        got = list(inspect.signature(getattr(ours, meth)).parameters)
+        assert got[:len(want)] == want, (meth, got, want)
+
+
 def test_fma_exp2_method():
     """The exponent-split + degree-3 polynomial 2^x of the prefill kernel
     (common.cuh ex2_fma), restated in float32 numpy: relative error below
@@ -139,3 +155,54 @@ def test_fma_exp2_method():
     rel = np.abs(res[ok].astype(np.float64) / np.exp2(x[ok].astype(np.float64)) - 1)
     assert rel.max() < 1e-4
     assert res[~ok].max() < 1e-37
+
+
+def test_graph_runner_bucket_choice():
+    from qwen3_engine_from_scratch_b200.graph_runner import bucket_for, DEFAULT_BUCKETS
+    assert DEFAULT_BUCKETS[-1] == 256
+    assert bucket_for(DEFAULT_BUCKETS, 0) == 1
+    assert bucket_for(DEFAULT_BUCKETS, 1) == 1
+    assert bucket_for(DEFAULT_BUCKETS, 3) == 4
+    assert bucket_for(DEFAULT_BUCKETS, 129) == 256
+    assert bucket_for((1, 2, 4, 8), 8) == 8
+    with pytest.raises(ValueError):
+        bucket_for(DEFAULT_BUCKETS, 257)
+    with pytest.raises(ValueError):
+        bucket_for(DEFAULT_BUCKETS, -1)
+
+
+def test_graph_runner_packs_host_inputs_with_dummy_rows():
+    from qwen3_engine_from_scratch_b200.graph_runner import pack_host_inputs
+    ids = np.full(8, -7, np.int64)
+    pos = np.full(8, -7, np.int64)
+    rows = np.full(8, -7, np.int32)
+    k = pack_host_inputs(ids, pos, rows, torch.tensor([[3], [9], [4]]), [10, 20, 30],
+                         np.array([5, 6, 7]), dummy_row=99)
+    assert k == 3
+    assert ids.tolist() == [3, 9, 4, 0, 0, 0, 0, 0]
+    assert pos.tolist() == [10, 20, 30, 0, 0, 0, 0, 0]
+    assert rows.tolist() == [5, 6, 7, 99, 99, 99, 99, 99]
+    with pytest.raises(ValueError):
+        pack_host_inputs(ids, pos, rows, [1, 2], [1], [1, 2], dummy_row=0)
+    with pytest.raises(ValueError):
+        pack_host_inputs(ids[:2], pos[:2], rows[:2], [1, 2, 3], [1, 2, 3], [1, 2, 3], 0)
+
+
+def test_kv_pool_blocks_from_free_memory():
+    from qwen3_engine_from_scratch_b200.graph_runner import kv_pool_blocks
+    # Qwen3-0.6B: 28 layers x 8 kv heads x 16 x 128 bf16, K and V: 1,835,008 B per block
+    per_block = 2 * 28 * 8 * 16 * 128 * 2
+    free = 170 * (1 << 30)
+    n = kv_pool_blocks(28, 8, 128, free_bytes=free, fraction=0.9, reserve_bytes=4 << 30)
+    assert n == (int(free * 0.9) - (4 << 30)) // per_block
+    assert kv_pool_blocks(28, 8, 128, free_bytes=1 << 30) == 0
+    assert kv_pool_blocks(28, 8, 128, dtype=torch.float32, free_bytes=free, fraction=1.0,
+                          reserve_bytes=0) == free // (2 * per_block)
+
+
+def test_graph_runner_rejects_bad_setup():
+    from qwen3_engine_from_scratch_b200.graph_runner import GraphRunner
+    with pytest.raises(ValueError):
+        GraphRunner(None, None, [], buckets=())
+    with pytest.raises(AssertionError):
+        GraphRunner(None, None, [object()] * 3, buckets=(1, 2, 4))
