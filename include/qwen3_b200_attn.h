@@ -160,6 +160,33 @@ int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                       int32_t* dev_status, void* stream);
 
 /*
+ * Decode step of one layer with the KV write fused in: replaces the pair
+ * update_kv_batch_triton + paged_attention_decode_triton that
+ * triton_paged_attention_decode_batch issues (qwen3/kernels/paged_attention.py:
+ * 222-289, the write :292-377).  k_new / v_new (batch, num_kv_heads, head_dim)
+ * bf16, strides (batch, head), are stored at position seq_lens[row_ids[b]] of
+ * the pool (k_pool / v_pool: the layer's first element, writable) exactly as
+ * b200_kv_scatter_rows with n_tokens == 1 stores them, and the decode then
+ * attends over seq_lens[row] + 1 tokens, the new one included; one launch.
+ * All other arguments, the workspace and the results as b200_paged_decode.
+ * A bad block-table entry for the new position sets B200_DEV_BAD_PAGE and
+ * skips the store.
+ */
+int b200_paged_decode_kv_write(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                               const void* k_new, int64_t k_new_stride_b, int64_t k_new_stride_h,
+                               const void* v_new, int64_t v_new_stride_b, int64_t v_new_stride_h,
+                               void* k_pool, void* v_pool,
+                               int64_t kv_stride_blk, int64_t kv_stride_h, int64_t kv_stride_slot,
+                               const int32_t* block_table, int64_t bt_stride_row,
+                               const int32_t* seq_lens, const int32_t* row_ids,
+                               void* out, int64_t out_stride_b, int64_t out_stride_h,
+                               int batch, int num_heads, int num_kv_heads, int head_dim,
+                               int block_size, int num_blocks, int max_pages, int max_requests,
+                               float scale, int pages_per_split,
+                               void* workspace, size_t workspace_bytes,
+                               int32_t* dev_status, void* stream);
+
+/*
  * Paged decode without a caller-provided workspace (allocation-free variant).
  * No counterpart in the reference: its Triton decode needs no workspace, and
  * the split-K design here does.  For callers that cannot allocate device

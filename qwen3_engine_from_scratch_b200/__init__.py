@@ -24,6 +24,7 @@ from .ops import (  # noqa: F401
     flash_attention_prefill,
     flash_attention_prefill_batched,
     paged_decode,
+    paged_decode_kv_write,
     kv_scatter_rows,
     kv_scatter_slots,
     qk_norm_rope_kv_write,

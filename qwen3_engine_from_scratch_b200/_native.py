@@ -63,6 +63,11 @@ SIGNATURES = {
                                _P, _I64, _P, _P, _P, _I64, _I64,
                                _I, _I, _I, _I, _I, _I, _I, _I, _F, _I,
                                _P, _SZ, _P, _P]),
+    "b200_paged_decode_kv_write": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,
+                                        _P, _P, _I64, _I64, _I64,
+                                        _P, _I64, _P, _P, _P, _I64, _I64,
+                                        _I, _I, _I, _I, _I, _I, _I, _I, _F, _I,
+                                        _P, _SZ, _P, _P]),
     "b200_paged_decode_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64,
                                        _P, _I64, _P, _P, _P, _I64, _I64,
                                        _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P]),

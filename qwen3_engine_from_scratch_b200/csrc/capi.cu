@@ -79,7 +79,7 @@ const char* b200_status_string(int status) {
   }
 }
 
-int b200_abi_version(void) { return 100; }
+int b200_abi_version(void) { return 101; }
 
 const char* b200_last_cuda_error_string(void) {
   const cudaError_t e = b200host::last_cuda_error();

@@ -33,6 +33,15 @@
 //   mma with V^T fragments from ldmatrix.trans.  The rescale factor of a head
 //   lives in the same lane as that head's accumulator columns, so no shuffle
 //   is needed for it.
+//
+// Fused KV write (b200_paged_decode_kv_write)
+//   The step's new K/V row of (request, kv head) belongs at position
+//   seq_lens[row] of the pool, inside the sequence's last page.  The CTA whose
+//   split holds that page stores the two 256-byte rows first (one 16-byte
+//   chunk per thread, the range checks of the KV write kernel), orders the
+//   stores before its own tensor loads with a generic-to-async proxy fence and
+//   a CTA barrier, and then reads the page like any other.  No other CTA reads
+//   that page, so one launch replaces the KV write launch and the decode.
 #include <math.h>
 
 #include <mutex>
@@ -77,6 +86,13 @@ struct DecodeArgs {
   int pages_per_split, max_splits;
   float scale_log2;
   int32_t* dev_status;
+  // fused KV write (k_new == nullptr: none)
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  int64_t kn_b, kn_h, vn_b, vn_h;
+  __nv_bfloat16* k_pool;
+  __nv_bfloat16* v_pool;
+  int64_t kv_blk, kv_h, kv_slot;
 };
 
 // Visible pages of request b: L = seq_lens[row] + 1 tokens (the current token
@@ -140,6 +156,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem + warp * kStages * kSlotBytes;
 
+  if (a.k_new != nullptr && p_end == npages && err == 0 && threadIdx.x < 32) {
+    // fused KV write of this step's token (position L - 1, in the last page):
+    // threads 0-15 store the K row, 16-31 the V row, 16 bytes each
+    const int pos = L - 1;
+    const int ph = a.block_table[static_cast<int64_t>(row) * a.bt_row + pos / kBS];
+    if (ph < 0 || ph >= a.num_blocks) {
+      if (threadIdx.x == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
+    } else {
+      const int i = threadIdx.x & 15;
+      const bool is_v = threadIdx.x >= 16;
+      const __nv_bfloat16* src = is_v ? a.v_new + b * a.vn_b + hkv * a.vn_h
+                                      : a.k_new + b * a.kn_b + hkv * a.kn_h;
+      __nv_bfloat16* dst = (is_v ? a.v_pool : a.k_pool) + static_cast<int64_t>(ph) * a.kv_blk +
+                           hkv * a.kv_h + (pos % kBS) * a.kv_slot;
+      *reinterpret_cast<uint4*>(dst + 8 * i) = *reinterpret_cast<const uint4*>(src + 8 * i);
+      // the stores above, then this CTA's tensor (async-proxy) loads of the page
+      b200::fence_proxy_async_global();
+    }
+  }
   if (threadIdx.x == 0) {
     b200::prefetch_tensormap(&kmap);
     b200::prefetch_tensormap(&vmap);
@@ -423,16 +458,19 @@ extern "C" size_t b200_paged_decode_workspace_size(int batch, int num_heads, int
   return kCounterBytes + static_cast<size_t>(batch) * num_heads * ms * (kD + 2) * sizeof(float);
 }
 
-extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
-                                 const void* k_pool, const void* v_pool, int64_t kv_stride_blk,
-                                 int64_t kv_stride_h, int64_t kv_stride_slot,
-                                 const int32_t* block_table, int64_t bt_stride_row,
-                                 const int32_t* seq_lens, const int32_t* row_ids, void* out,
-                                 int64_t out_stride_b, int64_t out_stride_h, int batch,
-                                 int num_heads, int num_kv_heads, int head_dim, int block_size,
-                                 int num_blocks, int max_pages, int max_requests, float scale,
-                                 int pages_per_split, void* workspace, size_t workspace_bytes,
-                                 int32_t* dev_status, void* stream) {
+namespace {
+
+// Shared by the decode entry points; k_new == nullptr: no fused KV write.
+int launch_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
+                  int64_t kn_stride_b, int64_t kn_stride_h, const void* v_new,
+                  int64_t vn_stride_b, int64_t vn_stride_h, const void* k_pool,
+                  const void* v_pool, int64_t kv_stride_blk, int64_t kv_stride_h,
+                  int64_t kv_stride_slot, const int32_t* block_table, int64_t bt_stride_row,
+                  const int32_t* seq_lens, const int32_t* row_ids, void* out,
+                  int64_t out_stride_b, int64_t out_stride_h, int batch, int num_heads,
+                  int num_kv_heads, int head_dim, int block_size, int num_blocks, int max_pages,
+                  int max_requests, float scale, int pages_per_split, void* workspace,
+                  size_t workspace_bytes, int32_t* dev_status, void* stream) {
   if (batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || max_pages <= 0 ||
       max_requests <= 0 || bt_stride_row <= 0)
     return B200_ERR_INVALID_ARGUMENT;
@@ -454,6 +492,12 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
                              kv_stride_blk, kv_stride_h, kv_stride_slot};
   for (int64_t s : strides)
     if (!mult8(s)) return B200_ERR_ALIGNMENT;
+  if (k_new != nullptr) {
+    if (v_new == nullptr) return B200_ERR_INVALID_ARGUMENT;
+    if (!b200host::aligned16(k_new) || !b200host::aligned16(v_new) || !mult8(kn_stride_b) ||
+        !mult8(kn_stride_h) || !mult8(vn_stride_b) || !mult8(vn_stride_h))
+      return B200_ERR_ALIGNMENT;
+  }
 
   const int ms = max_splits_for(max_pages, pages_per_split);
   if (ms > 65535) return B200_ERR_INVALID_ARGUMENT;
@@ -510,6 +554,17 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
   a.max_splits = ms;
   a.scale_log2 = scale * kLog2e;
   a.dev_status = dev_status;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.kn_b = kn_stride_b;
+  a.kn_h = kn_stride_h;
+  a.vn_b = vn_stride_b;
+  a.vn_h = vn_stride_h;
+  a.k_pool = static_cast<__nv_bfloat16*>(const_cast<void*>(k_pool));
+  a.v_pool = static_cast<__nv_bfloat16*>(const_cast<void*>(v_pool));
+  a.kv_blk = kv_stride_blk;
+  a.kv_h = kv_stride_h;
+  a.kv_slot = kv_stride_slot;
 
   int st = ensure_smem_attr(b200host::current_device());
   if (st != B200_OK) return st;
@@ -517,4 +572,42 @@ extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_st
   dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(ms));
   paged_decode_split_kernel<<<grid, kThreads, kSmemBytes, s>>>(kmap, vmap, a);
   return b200host::status_from_cuda(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int b200_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                 const void* k_pool, const void* v_pool, int64_t kv_stride_blk,
+                                 int64_t kv_stride_h, int64_t kv_stride_slot,
+                                 const int32_t* block_table, int64_t bt_stride_row,
+                                 const int32_t* seq_lens, const int32_t* row_ids, void* out,
+                                 int64_t out_stride_b, int64_t out_stride_h, int batch,
+                                 int num_heads, int num_kv_heads, int head_dim, int block_size,
+                                 int num_blocks, int max_pages, int max_requests, float scale,
+                                 int pages_per_split, void* workspace, size_t workspace_bytes,
+                                 int32_t* dev_status, void* stream) {
+  return launch_decode(q, q_stride_b, q_stride_h, nullptr, 0, 0, nullptr, 0, 0, k_pool, v_pool,
+                       kv_stride_blk, kv_stride_h, kv_stride_slot, block_table, bt_stride_row,
+                       seq_lens, row_ids, out, out_stride_b, out_stride_h, batch, num_heads,
+                       num_kv_heads, head_dim, block_size, num_blocks, max_pages, max_requests,
+                       scale, pages_per_split, workspace, workspace_bytes, dev_status, stream);
+}
+
+extern "C" int b200_paged_decode_kv_write(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
+    int64_t k_new_stride_b, int64_t k_new_stride_h, const void* v_new, int64_t v_new_stride_b,
+    int64_t v_new_stride_h, void* k_pool, void* v_pool, int64_t kv_stride_blk,
+    int64_t kv_stride_h, int64_t kv_stride_slot, const int32_t* block_table,
+    int64_t bt_stride_row, const int32_t* seq_lens, const int32_t* row_ids, void* out,
+    int64_t out_stride_b, int64_t out_stride_h, int batch, int num_heads, int num_kv_heads,
+    int head_dim, int block_size, int num_blocks, int max_pages, int max_requests, float scale,
+    int pages_per_split, void* workspace, size_t workspace_bytes, int32_t* dev_status,
+    void* stream) {
+  if (batch > 0 && (k_new == nullptr || v_new == nullptr)) return B200_ERR_INVALID_ARGUMENT;
+  return launch_decode(q, q_stride_b, q_stride_h, k_new, k_new_stride_b, k_new_stride_h, v_new,
+                       v_new_stride_b, v_new_stride_h, k_pool, v_pool, kv_stride_blk,
+                       kv_stride_h, kv_stride_slot, block_table, bt_stride_row, seq_lens, row_ids,
+                       out, out_stride_b, out_stride_h, batch, num_heads, num_kv_heads, head_dim,
+                       block_size, num_blocks, max_pages, max_requests, scale, pages_per_split,
+                       workspace, workspace_bytes, dev_status, stream);
 }

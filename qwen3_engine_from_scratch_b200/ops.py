@@ -43,6 +43,7 @@ __all__ = [
     "flash_attention_prefill",
     "flash_attention_prefill_batched",
     "paged_decode",
+    "paged_decode_kv_write",
     "kv_scatter_rows",
     "kv_scatter_slots",
     "qk_norm_rope_kv_write",
@@ -369,6 +370,58 @@ def paged_decode(q, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids, scale
     return out
 
 
+def paged_decode_kv_write(q, k_new, v_new, k_buffer, v_buffer, block_table_2d, seq_lens, row_ids,
+                          scale, out=None, pages_per_split=0):
+    """One layer's decode step in one launch: the KV write of the new token
+    (``kv_scatter_rows`` with one token) fused into the split-K decode.
+
+    q: (B, H, D) bf16; k_new/v_new: (B, Hkv, D) bf16 (strided views allowed);
+    k_buffer/v_buffer: (num_blocks, Hkv, 16, D) layer views of the pool
+    (``pool.k_buffer[:, layer]``), written at position ``seq_lens[row]``.
+    Returns (B, H, D) bf16, attending over ``seq_lens[row] + 1`` tokens.
+    """
+    assert q.dim() == 3, "q must be (B, num_heads, head_dim)"
+    assert q.dtype == torch.bfloat16, "b200 decode supports bf16 only"
+    assert k_new.dtype == torch.bfloat16 and v_new.dtype == torch.bfloat16, \
+        "b200 decode supports bf16 only"
+    assert k_buffer.dim() == 4, "k_buffer must be a (num_blocks, Hkv, block_size, D) layer view"
+    _check_pool(k_buffer, v_buffer)
+    _check_table(block_table_2d, seq_lens, row_ids)
+    B, H, D = q.shape
+    nb, Hkv, bs, d_p = k_buffer.shape
+    assert d_p == D, "head_dim mismatch between q and the pool"
+    assert k_buffer.stride() == v_buffer.stride(), "k/v pool views must share strides"
+    assert row_ids.numel() == B, "row_ids must have one entry per request"
+    assert k_new.shape == (B, Hkv, D) and v_new.shape == (B, Hkv, D), \
+        "k_new/v_new must be (B, num_kv_heads, head_dim)"
+    q = _vec_ready(q, 0, 1)
+    k_new = _vec_ready(k_new, 0, 1)
+    v_new = _vec_ready(v_new, 0, 1)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=torch.bfloat16, device=q.device)
+    max_pages = block_table_2d.shape[1]
+    lib = _native.load()
+    if pages_per_split <= 0:
+        pages_per_split = _default_split(lib, B, Hkv, max_pages)
+    ws_bytes = lib.b200_paged_decode_workspace_size(B, H, max_pages, pages_per_split)
+    ws = _decode_workspace(q.device, ws_bytes) if ws_bytes else None
+    st = lib.b200_paged_decode_kv_write(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        v_new.data_ptr(), v_new.stride(0), v_new.stride(1),
+        k_buffer.data_ptr(), v_buffer.data_ptr(),
+        k_buffer.stride(0), k_buffer.stride(1), k_buffer.stride(2),
+        block_table_2d.data_ptr(), block_table_2d.stride(0),
+        seq_lens.data_ptr(), row_ids.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        B, H, Hkv, D, bs, nb, max_pages, block_table_2d.shape[0],
+        float(scale), int(pages_per_split),
+        ws.data_ptr() if ws is not None else None, ws_bytes,
+        _status_ptr(q.device), _stream())
+    _native.check(st, "b200_paged_decode_kv_write")
+    return out
+
+
 def paged_attention_decode_triton(q, k_buffer, v_buffer, block_table_2d, seq_lens_full, row_ids,
                                   block_size):
     """Bare decode entry (qwen3/kernels/paged_attention.py:132-178).
@@ -424,10 +477,9 @@ def triton_paged_attention_decode_batch(q, k_new, v_new, kv_caches, layer_idx, s
             c.reserve_next()
         row_ids = torch.tensor([c.row_id for c in kv_caches], dtype=torch.int32, device=q.device)
     pool = _pool_of(kv_caches[0])
-    kv_scatter_rows(k_new, v_new, pool.k_buffer, pool.v_buffer, pool.seq_lens, pool.block_table_2d,
-                    row_ids, layer_idx)
-    out = paged_decode(q.squeeze(2), pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
-                       pool.block_table_2d, pool.seq_lens, row_ids, scaling)
+    out = paged_decode_kv_write(q.squeeze(2), k_new.squeeze(2), v_new.squeeze(2),
+                                pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
+                                pool.block_table_2d, pool.seq_lens, row_ids, scaling)
     num_heads, head_dim = q.shape[1], q.shape[3]
     return out.reshape(B, 1, num_heads * head_dim)
 
@@ -438,10 +490,9 @@ def triton_paged_attention_decode(q, k_new, v_new, kv_cache, layer_idx, scaling)
     assert q.dtype == torch.bfloat16, "decode kernel supports bf16 only"
     row_ids = _row_ids_of(kv_cache, q.device)
     pool = _pool_of(kv_cache)
-    kv_scatter_rows(k_new, v_new, pool.k_buffer, pool.v_buffer, pool.seq_lens, pool.block_table_2d,
-                    row_ids, layer_idx)
-    out = paged_decode(q.squeeze(2), pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
-                       pool.block_table_2d, pool.seq_lens, row_ids, scaling)
+    out = paged_decode_kv_write(q.squeeze(2), k_new.squeeze(2), v_new.squeeze(2),
+                                pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
+                                pool.block_table_2d, pool.seq_lens, row_ids, scaling)
     B, num_heads, head_dim = q.shape[0], q.shape[1], q.shape[3]
     return out.reshape(B, 1, num_heads * head_dim)
 

@@ -292,3 +292,113 @@ def test_decode_argument_errors(cuda, native_lib):
         qb.triton_paged_attention_decode_batch(torch.cat([q[:, :, None]] * 2, 2), q, q, caches, 0, 1.0)
     with pytest.raises(AssertionError):   # len(kv_caches) != B
         qb.triton_paged_attention_decode_batch(q[:, :, None], q, q, caches[:1], 0, 1.0)
+
+
+def _fused_state(device, B=64, Hkv=8, H=16, layers=2, max_len=2000, seed=77):
+    """A 2-layer pool filled with N(0,1) everywhere (so a stale read of the new
+    token's slot changes the result), random page placement, row slots that
+    are not 0..B-1, lengths including page-boundary cases."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    lens = torch.randint(1, max_len, (B,), generator=g, device=device).cpu().numpy()
+    lens[:4] = [1, 16, 17, 33]                          # seq_lens 0, 15, 16, 32: page starts
+    spare = 4                                           # room for a few more steps
+    max_pages = (max_len + spare + 15) // 16 + 1
+    need = int(sum((L + spare + 15) // 16 for L in lens))
+    num_blocks = need + 64
+    perm = torch.randperm(num_blocks, generator=g, device=device).cpu().numpy()
+    R = B + 5
+    rows = (np.arange(B) * 11 + 3) % R
+    bt = np.full((R, max_pages), -1, np.int32)
+    used = 0
+    for b in range(B):
+        n = (int(lens[b]) + spare + 15) // 16
+        bt[rows[b], :n] = perm[used:used + n]
+        used += n
+    seq = np.zeros(R, np.int32)
+    seq[rows] = lens - 1
+    D = 128
+    kp = torch.randn(num_blocks, layers, Hkv, 16, D, generator=g, device=device).to(torch.bfloat16)
+    vp = torch.randn(num_blocks, layers, Hkv, 16, D, generator=g, device=device).to(torch.bfloat16)
+    q = torch.randn(B, H, D, generator=g, device=device).to(torch.bfloat16)
+    # k/v new as strided views of one fused (B, H + 2 Hkv, D) projection
+    qkv = torch.randn(B, H + 2 * Hkv, D, generator=g, device=device).to(torch.bfloat16)
+    return dict(q=q, k_new=qkv[:, H:H + Hkv], v_new=qkv[:, H + Hkv:], kp=kp, vp=vp,
+                bt=torch.from_numpy(bt).to(device), seq=torch.from_numpy(seq).to(device),
+                rows=torch.from_numpy(rows.astype(np.int32)).to(device))
+
+
+@pytest.mark.parametrize("pps", [0, 1, 4, 128])
+def test_fused_kv_write_equals_write_then_decode(pps, cuda, native_lib):
+    """b200_paged_decode_kv_write == b200_kv_scatter_rows + b200_paged_decode,
+    bit for bit: the outputs and every byte of both layers of the pool."""
+    import qwen3_engine_from_scratch_b200 as qb
+    w = _fused_state(cuda)
+    scale = 128 ** -0.5
+    for layer in (1, 0):
+        ka, va = w["kp"].clone(), w["vp"].clone()
+        kb, vb = w["kp"].clone(), w["vp"].clone()
+        qb.clear_device_status()
+        qb.kv_scatter_rows(w["k_new"][:, :, None], w["v_new"][:, :, None], ka, va, w["seq"],
+                           w["bt"], w["rows"], layer)
+        ref = qb.paged_decode(w["q"], ka[:, layer], va[:, layer], w["bt"], w["seq"], w["rows"],
+                              scale, pages_per_split=pps)
+        out = qb.paged_decode_kv_write(w["q"], w["k_new"], w["v_new"], kb[:, layer], vb[:, layer],
+                                       w["bt"], w["seq"], w["rows"], scale, pages_per_split=pps)
+        torch.cuda.synchronize()
+        qb.check_device_status()
+        assert torch.equal(out, ref)
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+        # the new rows really landed (the pool held other values there before)
+        assert not torch.equal(ka, w["kp"])
+
+
+def test_fused_kv_write_repeated_and_in_graph(cuda, native_lib):
+    """Several fused steps in a row (seq_lens advancing, as the engine does
+    between steps) match the unfused pair, also when captured in a CUDA graph."""
+    import qwen3_engine_from_scratch_b200 as qb
+    w = _fused_state(cuda, B=32, max_len=600, seed=5)
+    scale = 128 ** -0.5
+    ka, va = w["kp"].clone(), w["vp"].clone()
+    kb, vb = w["kp"].clone(), w["vp"].clone()
+    seq_a, seq_b = w["seq"].clone(), w["seq"].clone()
+    out_b = torch.empty_like(w["q"])
+
+    def fused():
+        qb.paged_decode_kv_write(w["q"], w["k_new"], w["v_new"], kb[:, 0], vb[:, 0], w["bt"],
+                                 seq_b, w["rows"], scale, out=out_b)
+
+    fused()                                   # warm-up (workspace) before capture
+    torch.cuda.synchronize()
+    kb.copy_(w["kp"])
+    vb.copy_(w["vp"])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fused()
+    for step in range(3):
+        qb.kv_scatter_rows(w["k_new"][:, :, None], w["v_new"][:, :, None], ka, va, seq_a, w["bt"],
+                           w["rows"], 0)
+        ref = qb.paged_decode(w["q"], ka[:, 0], va[:, 0], w["bt"], seq_a, w["rows"], scale)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_b, ref), step
+        assert torch.equal(ka, kb) and torch.equal(va, vb), step
+        seq_a[w["rows"].long()] += 1
+        seq_b[w["rows"].long()] += 1
+    del graph
+
+
+def test_fused_kv_write_bad_page_flagged(cuda, native_lib):
+    """A -1 block-table entry at the new token's page: flagged, no store."""
+    import qwen3_engine_from_scratch_b200 as qb
+    w = _fused_state(cuda, B=8, max_len=300, seed=9)
+    bt = w["bt"].clone()
+    r0 = int(w["rows"][0])
+    pos = int(w["seq"][r0])
+    bt[r0, pos // 16] = -1
+    kb, vb = w["kp"].clone(), w["vp"].clone()
+    qb.clear_device_status()
+    qb.paged_decode_kv_write(w["q"], w["k_new"], w["v_new"], kb[:, 0], vb[:, 0], bt, w["seq"],
+                             w["rows"], 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert qb.device_status() & 0x2
+    qb.clear_device_status()
