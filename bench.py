@@ -534,7 +534,7 @@ def bench_sampling(device, steps=20, warmup=3):
     return res
 
 
-def run_prefill(args, rank, world, local_rank, steps, warmup):
+def run_prefill(args, rank, world, local_rank, steps, warmup, headline=False):
     """Config 3: varlen causal prefill of 32 packed sequences (+ the slot scatter of
     their K/V into a paged pool through a random slot_mapping), timed with CUDA events."""
     import torch
@@ -581,6 +581,9 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
     pa = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     pb = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     sb = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    clocks = ClockSampler(local_rank) if headline else None
+    if clocks is not None:
+        clocks.start()
     for i in range(steps):
         pa[i].record(stream)
         prefill()
@@ -588,6 +591,8 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
         ops.kv_scatter_slots(k, v, kp, vp, slots)
         sb[i].record(stream)
     torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.stop()
     qb.check_device_status(device)
     p_ms = sum(a.elapsed_time(b) for a, b in zip(pa, pb)) / steps
     s_ms = sum(a.elapsed_time(b) for a, b in zip(pb, sb)) / steps
@@ -595,6 +600,40 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
     sbytes = T * Hkv * D * 2 * 2 * 2 + T * 8
     peaks, src = read_peaks()
     tflops = flops / (p_ms / 1e3) / 1e12
+    extra = {}
+    if headline:
+        # e2e through the public entry point: pinned host q/k/v up, the prefill, output down
+        hq, hk, hv = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+        hout = torch.empty((T, H, D), dtype=torch.bfloat16).pin_memory()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            o = ops.flash_attention_prefill(dq, dk, dv, cu, scale, H, Hkv, D, max_seqlen=max_len)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(max(2, warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(stream)
+        for _ in range(steps):
+            e2e_step()
+        eb.record(stream)
+        torch.cuda.synchronize()
+        e_ms = ea.elapsed_time(eb) / steps
+        extra["e2e"] = {"value": round(flops / (e_ms / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+                        "ms_per_step": round(e_ms, 4),
+                        "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 2),
+                        "d2h_bytes_per_step": int(hout.numel() * 2),
+                        "api": "flash_attention_prefill (qwen3/kernels/flash_attention_varlen.py:"
+                               "126-194 signature, max_seqlen given: no host sync) with q/k/v "
+                               "copied from pinned host memory and the output copied back, every "
+                               "step"}
+        extra["clocks"] = clocks.summary()
+        extra["gpu_launches"] = steps * 2   # the prefill and the slot-mode KV write per step
     prologue = bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks)
     chunked = bench_paged_prefill(torch, ops, device, rank, H, Hkv, D, steps, warmup, peaks)
     return {"workload": w["name"], "tokens": T, "sequences": len(lens),
@@ -610,7 +649,7 @@ def run_prefill(args, rank, world, local_rank, steps, warmup):
                         "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
             "prologue": prologue,
             "paged_prefill": chunked,
-            "gpu_launches_per_step": 2}
+            "gpu_launches_per_step": 2, **extra}
 
 
 def bench_paged_prefill(torch, ops, device, rank, H, Hkv, D, steps, warmup, peaks):
@@ -846,10 +885,60 @@ def cpu_baseline(w, budget_s=20.0, procs=1):
                       f"oracle.paged_decode (numpy fp32 restatement of qwen3/paged_attention.py)"}
 
 
+def prefill_cpu_sample(w, budget_s):
+    """Oracle varlen prefill (numpy fp32, the reference's _standard_attention
+    semantics) on the shortest-first sequences of the config-3 batch until about
+    ``budget_s`` seconds of CPU work; returns (flops, seconds, sequences)."""
+    from oracle import attention as oa
+    lens = np.asarray(w["lens"], dtype=np.int64)
+    H, Hkv, D = w["H"], w["Hkv"], HEAD_DIM
+    rng = np.random.default_rng(3)
+    order = np.argsort(lens, kind="stable")
+    flops = 0
+    used = []
+    t0 = time.perf_counter()
+    for i in order:
+        L = int(lens[i])
+        q = rng.standard_normal((L, H, D), dtype=np.float32)
+        k = rng.standard_normal((L, Hkv, D), dtype=np.float32)
+        v = rng.standard_normal((L, Hkv, D), dtype=np.float32)
+        oa.varlen_prefill(q, k, v, np.array([0, L]), D ** -0.5)
+        flops += prefill_flops([L], H)
+        used.append(L)
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return flops, time.perf_counter() - t0, used
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference algorithm (oracle port) on the host cores."""
     if rank != 0:
         return None
+    if args.config == "c3":
+        w = workload("c3", 0, 1)
+        threads = max(1, os.cpu_count() or 1)
+        budget = 150.0 / max(1, args.steps + args.warmup)
+        fl, dt, used = 0, 0.0, []
+        for i in range(args.warmup + args.steps):
+            f_, d_, u_ = prefill_cpu_sample(w, budget)
+            if i >= args.warmup:
+                fl, dt, used = fl + f_, dt + d_, u_
+        value = fl / dt / 1e12
+        sample = (f"{len(used)}/{len(w['lens'])} sequences of the config-3 batch per step "
+                  f"(shortest first, lengths {min(used)}-{max(used)}), oracle.varlen_prefill (numpy "
+                  f"fp32 restatement of the reference's causal _standard_attention), numpy BLAS "
+                  f"threads on {threads} host cores")
+        return {
+            "metric": "varlen_prefill_tflops", "value": round(value, 6), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": {"workload": w["name"]},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
     w = workload(args.config, 0, 1)
     lens = np.asarray(w["lens"], dtype=np.int64)
     H, Hkv = w["H"], w["Hkv"]
@@ -924,15 +1013,31 @@ def main():
     try:
         if args.config == "c3":
             torch.cuda.set_device(local_rank)
-            r = run_prefill(args, rank, world, local_rank, steps=args.steps, warmup=args.warmup)
+            r = run_prefill(args, rank, world, local_rank, steps=args.steps, warmup=args.warmup,
+                            headline=True)
             line = None
             if rank == 0:
                 line = {"metric": "varlen_prefill_tflops", "value": r["tflops"], "unit": "TFLOP/s",
                         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                         "ms_per_step": r["ms_per_prefill"], "higher_is_better": True,
                         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                        "data": "synthetic", "config": {"workload": r["workload"]},
-                        "roofline": r["roofline"], "detail": r}
+                        "data": "synthetic: N(0,1) q/k/v, q/k RMS-normed + RoPE theta 1e6",
+                        "config": {"workload": r["workload"], "sequences": r["sequences"],
+                                   "tokens": r["tokens"], "lengths": r["lengths"],
+                                   "heads": r["heads"], "head_dim": HEAD_DIM,
+                                   "l2": "inputs larger than L2 (q/k/v 259.6 MB per step)",
+                                   "parallelism": f"request-sharded x{world}" if world > 1
+                                   else "single GPU"},
+                        "roofline": r["roofline"], "e2e": r["e2e"], "clocks": r["clocks"],
+                        "gpu_launches": r["gpu_launches"], "detail": r}
+                if world == 1 and not args.no_cpu_baseline:
+                    fl, dt, used = prefill_cpu_sample(workload("c3", 0, 1), args.cpu_budget)
+                    line["cpu_baseline"] = {
+                        "value": round(fl / dt / 1e12, 6), "unit": "TFLOP/s",
+                        "cores": max(1, os.cpu_count() or 1), "kind": "port",
+                        "sample": f"{len(used)}/32 sequences (shortest first, lengths "
+                                  f"{min(used)}-{max(used)}) in {dt:.1f} s, oracle.varlen_prefill "
+                                  f"(numpy fp32, BLAS threads on the host cores)"}
         else:
             line = run_b200(args, rank, world, local_rank)
         if line is not None:
