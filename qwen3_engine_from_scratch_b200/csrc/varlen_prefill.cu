@@ -85,7 +85,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxSeqs = 256;               // sequences per launch (the host splits larger batches)
 constexpr int kMaxTiles = 2048;             // 128-row tiles per sequence (max_seqlen <= 262144)
 constexpr int kRing = 4;                    // item-index ring between the scheduler and the roles
-constexpr int kRingConsumers = 2 + kSoftmaxThreads;  // V lane, MMA thread, softmax threads
+// V lane, store lane, MMA thread, softmax threads
+constexpr int kRingConsumers = 3 + kSoftmaxThreads;
 
 struct PrefillArgs {
   const int32_t* cu;
@@ -188,6 +189,7 @@ struct __align__(8) Barriers {
   uint64_t p_full[2];         // P_t(g) written over S_t(g), O_t rescaled
   uint64_t o_done[2];         // the item's last P_t.V done (O_t final)
   uint64_t o_free[2];         // the item's O_t was read by its softmax warps
+  uint64_t staged[2][2];      // [tile][item parity]: the tile's output rows are in its stage
   uint64_t ring_full[kRing], ring_empty[kRing];
   uint32_t tmem_base;
   int32_t error;
@@ -426,7 +428,8 @@ template <int FMA_PAIRS>
 __global__ void __launch_bounds__(kThreads, 1)
     varlen_prefill_kernel(const __grid_constant__ CUtensorMap tmq,
                           const __grid_constant__ CUtensorMap tmk,
-                          const __grid_constant__ CUtensorMap tmv, const PrefillArgs a) {
+                          const __grid_constant__ CUtensorMap tmv,
+                          const __grid_constant__ CUtensorMap tmo, const PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Barriers B;
   __shared__ WorkList W;
@@ -456,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_p = [&](int t) { return b200::smem_u32(&B.p_full[t]); };
   auto bar_od = [&](int t) { return b200::smem_u32(&B.o_done[t]); };
   auto bar_of = [&](int t) { return b200::smem_u32(&B.o_free[t]); };
+  auto bar_st = [&](int t, int n) { return b200::smem_u32(&B.staged[t][n & 1]); };
   auto bar_rf = [&](int n) { return b200::smem_u32(&B.ring_full[n & (kRing - 1)]); };
   auto bar_re = [&](int n) { return b200::smem_u32(&B.ring_empty[n & (kRing - 1)]); };
 
@@ -473,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       b200::mbar_init(bar_p(t), 128);
       b200::mbar_init(bar_od(t), 1);
       b200::mbar_init(bar_of(t), 128);
+      b200::mbar_init(bar_st(t, 0), 128);
+      b200::mbar_init(bar_st(t, 1), 128);
     }
     for (int r = 0; r < kRing; ++r) {
       b200::mbar_init(bar_rf(r), 1);
@@ -547,6 +553,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+    } else if (lane == 2) {
+      // store lane: sends each finished tile's output (staged by its softmax
+      // threads in the stage of the item's last K tile for tile 0, of its last
+      // V tile for tile 1) to global memory with two TMA stores, and hands the
+      // stage back to its producer once the stores have read it
+      b200::prefetch_tensormap(&tmo);
+      int gs = 0;  // steps of this CTA before the current item
+      bool ok = true;
+      for (int n = 0; ok; ++n) {
+        const int k = next_item(n, ok);
+        if (!ok || k < 0) break;
+        const Item it = decode_item(a, W, k);
+        const int g_last = gs + it.n_kv - 1;
+        gs += it.n_kv;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!(ok = wait_or_flag(bar_st(t, n), (n >> 1) & 1, &B, a.dev_status))) break;
+          const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
+          if (it.m0[t] + kBM <= it.len) {
+            b200::tma_store_3d(&tmo, stage, 0, it.h[t], it.start + it.m0[t]);
+            b200::tma_store_3d(&tmo, stage + kKVBlock, 64, it.h[t], it.start + it.m0[t]);
+            b200::bulk_commit_group();
+            b200::bulk_wait_group_read0();
+          }
+          mbar_arrive(t == 0 ? bar_ke(g_last & 1) : bar_ve(g_last & 1));
+        }
+      }
+      // the output stores are complete before the CTA ends
+      b200::bulk_wait_group0();
     } else if (lane == 1) {
       b200::prefetch_tensormap(&tmv);
       int vc = 0;
@@ -629,11 +663,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (!ok) break;
-          if (j < it.n_kv) {
-            umma_commit(bar_ke(gs & 1));
-            if (j == it.n_kv - 1) umma_commit(bar_qe);
-          }
-          if (j > 0) umma_commit(bar_ve(gp & 1));
+          // the stages of the item's last K and V tiles are released by the
+          // epilogue instead (it stages the output in them)
+          if (j < it.n_kv - 1) umma_commit(bar_ke(gs & 1));
+          if (j == it.n_kv - 1) umma_commit(bar_qe);
+          if (j > 0 && j < it.n_kv) umma_commit(bar_ve(gp & 1));
         }
         g += it.n_kv;
       }
@@ -782,7 +816,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kD / 32; ++c) tmem_wait_ld(ov + c * 32);
       tc_fence_before();
       mbar_arrive(bar_of(t));
-      if (qpos < it.len) {  // rows past the sequence are zeroed by the pass above
+      // Staging buffer of this tile: the stage of the item's last K tile for
+      // tile 0 (o_done of tile 0 covers every S of the item, tile 1's last
+      // included), the stage of its last V tile for tile 1 (o_done of tile 1
+      // covers both last P.V).  The store lane of the producer warp sends it
+      // out with TMA stores and returns the stage to its producer; the stage's
+      // next tile (the next item's second K / V tile) is needed only a step
+      // later.
+      const int g_last = g - 1;  // this CTA's step index of the item's last K/V tile
+      const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
+      if (it.m0[t] + kBM <= it.len) {
+        // a full tile: rows staged in the swizzled [128 rows][64 d] x 2 layout
+        // of a K/V tile (the TMA engine writes whole lines; the memory-
+        // instruction queue that the other tile's softmax and the MMA thread
+        // use carries a quarter of the requests of row-per-thread stores)
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c) {
+          const int e = 8 * c;
+          b200::st_shared_v4(stage + (c >> 3) * kKVBlock + r * 128 + (((c & 7) ^ (r & 7)) << 4),
+                             b200::pack_bf16x2(__uint_as_float(ov[e]) * inv,
+                                               __uint_as_float(ov[e + 1]) * inv),
+                             b200::pack_bf16x2(__uint_as_float(ov[e + 2]) * inv,
+                                               __uint_as_float(ov[e + 3]) * inv),
+                             b200::pack_bf16x2(__uint_as_float(ov[e + 4]) * inv,
+                                               __uint_as_float(ov[e + 5]) * inv),
+                             b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv,
+                                               __uint_as_float(ov[e + 7]) * inv));
+        }
+        b200::fence_proxy_async_smem();  // the rows, then the store lane's TMA stores
+        mbar_arrive(bar_st(t, n));
+      } else {
+        // the sequence's ragged last tile: each thread writes its own row
+        // (rows past the sequence are zeroed by the pass above, if asked)
+        mbar_arrive(bar_st(t, n));  // nothing staged: the stage goes straight back
+        if (qpos < it.len) {
         const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
                               static_cast<int64_t>(it.h[t]) * a.o_h;
@@ -807,6 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             v.w = b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv, __uint_as_float(ov[e + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + e) = v;
           }
+        }
         }
       }
     }
@@ -886,6 +955,7 @@ int encode_rows_map(CUtensorMap* map, const void* base, int heads, int tokens, i
 // Launches the kernel over `num_seqs` sequences, at most kMaxSeqs per launch;
 // `base` carries every field but the per-launch sequence slices.
 int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   const CUtensorMap& to,
                    PrefillArgs base, const int32_t* cu_seqlens, const int32_t* lens_opt,
                    const int32_t* row_ids, int num_seqs, void* stream) {
   int st = ensure_smem_attr(b200host::current_device());
@@ -902,11 +972,11 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
     a.num_seqs = num_seqs - s0 < kMaxSeqs ? num_seqs - s0 : kMaxSeqs;
     dim3 grid(static_cast<unsigned>(sms));  // one persistent CTA per SM
     switch (pairs) {
-      case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
-      default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, a); break;
+      case 0: varlen_prefill_kernel<0><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, to, a); break;
+      case 2: varlen_prefill_kernel<2><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, to, a); break;
+      case 3: varlen_prefill_kernel<3><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, to, a); break;
+      case 4: varlen_prefill_kernel<4><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, to, a); break;
+      default: varlen_prefill_kernel<1><<<grid, kThreads, kSmemBytes, cs>>>(tq, tk, tv, to, a); break;
     }
     st = b200host::status_from_cuda(cudaGetLastError());
     if (st != B200_OK) return st;
@@ -973,7 +1043,10 @@ extern "C" int b200_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_
   PrefillArgs a = base_args(out, o_stride_t, o_stride_h, num_heads, num_kv_heads, max_seqlen,
                             total_tokens, scale, work_counter, dev_status);
   a.zero_pad = zero_pad_rows != 0;
-  return launch_prefill(tq, tk, tv, a, cu_seqlens, seq_lens_opt, nullptr, num_seqs, stream);
+  CUtensorMap to;  // the output, in the boxes of a Q load
+  st = encode_rows_map(&to, out, num_heads, total_tokens, o_stride_t, o_stride_h, kBM);
+  if (st != B200_OK) return st;
+  return launch_prefill(tq, tk, tv, to, a, cu_seqlens, seq_lens_opt, nullptr, num_seqs, stream);
 }
 
 extern "C" int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
@@ -1041,5 +1114,8 @@ extern "C" int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_s
   a.num_blocks = num_blocks;
   a.max_pages = max_pages;
   a.max_requests = max_requests;
-  return launch_prefill(tq, tk, tv, a, cu_seqlens, nullptr, row_ids, num_seqs, stream);
+  CUtensorMap to;  // the output, in the boxes of a Q load
+  st = encode_rows_map(&to, out, num_heads, total_tokens, o_stride_t, o_stride_h, kBM);
+  if (st != B200_OK) return st;
+  return launch_prefill(tq, tk, tv, to, a, cu_seqlens, nullptr, row_ids, num_seqs, stream);
 }
