@@ -482,7 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int r = 0; r < kRing; ++r) {
       b200::mbar_init(bar_rf(r), 1);
-      b200::mbar_init(bar_re(r), kRingConsumers);
+      // (paged mode: the store lane has no work and does not read the ring)
+      b200::mbar_init(bar_re(r), a.paged ? kRingConsumers - 1 : kRingConsumers);
     }
     B.error = 0;
     b200::fence_mbar_init();
@@ -553,8 +554,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else if (lane == 2) {
-      // store lane: sends each finished tile's output (staged by its softmax
+    } else if (lane == 2 && !a.paged) {
+      // store lane (not in paged mode, whose epilogue writes rows directly
+      // and whose stages the MMA thread releases): sends each finished tile's output (staged by its softmax
       // threads in the stage of the item's last K tile for tile 0, of its last
       // V tile for tile 1) to global memory with two TMA stores, and hands the
       // stage back to its producer once the stores have read it
@@ -567,6 +569,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Item it = decode_item(a, W, k);
         const int g_last = gs + it.n_kv - 1;
         gs += it.n_kv;
+        // The lead of the softmax over this lane is bounded: the stage this
+        // lane returns for item n is the one the next item but one loads its
+        // second K / V tile into, so the softmax cannot complete a tile of
+        // item n + 2 before this lane has taken item n's.
         for (int t = 0; t < 2 && ok; ++t) {
           if (!(ok = wait_or_flag(bar_st(t, n), (n >> 1) & 1, &B, a.dev_status))) break;
           const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
@@ -664,10 +670,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           // the stages of the item's last K and V tiles are released by the
-          // epilogue instead (it stages the output in them)
-          if (j < it.n_kv - 1) umma_commit(bar_ke(gs & 1));
+          // store lane instead (the epilogue stages the output in them),
+          // except in paged mode, whose epilogue writes rows directly
+          if (j < it.n_kv - 1 || (a.paged && j < it.n_kv)) umma_commit(bar_ke(gs & 1));
           if (j == it.n_kv - 1) umma_commit(bar_qe);
-          if (j > 0 && j < it.n_kv) umma_commit(bar_ve(gp & 1));
+          if (j > 0 && (j < it.n_kv || a.paged)) umma_commit(bar_ve(gp & 1));
         }
         g += it.n_kv;
       }
@@ -825,7 +832,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // later.
       const int g_last = g - 1;  // this CTA's step index of the item's last K/V tile
       const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
-      if (it.m0[t] + kBM <= it.len) {
+      // (paged mode: every tile row by row; its K/V stages, filled from 16
+      // page boxes each, go back to their producers without waiting for this)
+      if (!a.paged && it.m0[t] + kBM <= it.len) {
         // a full tile: rows staged in the swizzled [128 rows][64 d] x 2 layout
         // of a K/V tile (the TMA engine writes whole lines; the memory-
         // instruction queue that the other tile's softmax and the MMA thread
@@ -849,7 +858,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         // the sequence's ragged last tile: each thread writes its own row
         // (rows past the sequence are zeroed by the pass above, if asked)
-        mbar_arrive(bar_st(t, n));  // nothing staged: the stage goes straight back
+        if (!a.paged) mbar_arrive(bar_st(t, n));  // nothing staged: the stage goes straight back
         if (qpos < it.len) {
         const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
