@@ -18,10 +18,13 @@
 //
 // Data movement
 //   Each page of one kv head is a contiguous 16 x 128 bf16 tile (4 KB) of K
-//   and one of V.  Lane 0 of a warp stages them into a per-warp ring of
+//   and one of V.  Lane 0 of a warp stages them into a per-warp ring of 2
 //   shared-memory slots with 4 TMA tensor loads (two 64-column boxes per
 //   tensor, 128-byte swizzle, L2 evict-first) that complete on the slot's
-//   mbarrier; all waits are bounded.
+//   mbarrier; all waits are bounded.  3 CTAs per SM (65 KB of slots each)
+//   keep up to 192 KB of loads in flight per SM; with more CTAs of fewer
+//   slots, one CTA's prologue or merge leaves less of the SM idle than with
+//   2 CTAs of 3 slots (measured: the 28-layer config-2 step 2.61 -> 2.52 ms).
 //
 // Math (per page, per warp; G = num_heads / num_kv_heads <= 8)
 //   S^T (16 tokens x 8 heads) = K (16 x 128) . Q^T (128 x 8): 8 x mma.m16n8k16,
@@ -54,7 +57,7 @@ constexpr int kD = 128;
 constexpr int kBS = 16;
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kPageBytes = kBS * kD * 2;  // 4096
 constexpr int kHalfBytes = kPageBytes / 2;
 constexpr int kSlotBytes = 2 * kPageBytes;
@@ -121,7 +124,7 @@ B200_DEVICE int request_pages(const DecodeArgs& a, int b, int& row, int& L, int&
   return npages;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     paged_decode_split_kernel(const __grid_constant__ CUtensorMap kmap,
                               const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -411,13 +414,15 @@ bool mult8(int64_t s) { return (s & 7) == 0; }
 int max_splits_for(int max_pages, int pps) { return (max_pages + pps - 1) / pps; }
 
 // Default split size: as many pages per CTA as possible (each split pays a
-// prologue, an epilogue and a partial to merge), but enough CTAs for about 4
-// per SM if the sequences fill half of the block table.  Measured on B200
-// (config 2: 512 pairs x 256 pages -> 110; config 4: 4096 pairs x 2048 pages
-// -> 128): 5,434 -> ~6,000 GB/s and 4,777 -> 7,031 GB/s against a fixed 16.
+// prologue, an epilogue and a partial to merge), but enough CTAs for about 6
+// per SM (two waves of the 3 resident ones) if the sequences fill half of the
+// block table.  Measured on B200 (config 2: 512 pairs x 256 pages -> 73;
+// config 4: 4096 pairs x 2048 pages -> 128): the 28-layer config-2 step at
+// 6.40 TB/s against 6.30 with 110 pages (8 slots per SM), and config 4 at
+// 7.07 TB/s.
 int default_pages_per_split(int batch, int num_kv_heads, int max_pages) {
   const int sms = b200host::sm_count(b200host::current_device());
-  const int64_t slots = 8 * static_cast<int64_t>(sms > 0 ? sms : 148);
+  const int64_t slots = 12 * static_cast<int64_t>(sms > 0 ? sms : 148);
   const int64_t pps =
       static_cast<int64_t>(batch) * num_kv_heads * static_cast<int64_t>(max_pages) / slots;
   return static_cast<int>(pps < kMinDefaultPagesPerSplit

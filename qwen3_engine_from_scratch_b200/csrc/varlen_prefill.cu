@@ -3,7 +3,7 @@
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
 // Persistent, one CTA per SM (192 KB of tiles in shared memory, all 512 TMEM
-// columns).  A work item is a PAIR of 128-row query tiles that read the same
+// columns, 10 warps).  A work item is a PAIR of 128-row query tiles that read the same
 // K/V rows: two query heads of one kv head at the same positions (GQA group
 // even), or two consecutive row tiles of one head (group odd).  Each 128-key
 // K/V tile is loaded once for both.  The two tiles ping-pong: while the
@@ -16,13 +16,18 @@
 //               64 columns of the same score buffer (tcgen05.st).  Its O row
 //               is rescaled only when the running max grew by more than 2^8
 //               (otherwise the stale max keeps every P <= 2^8).  After the
-//               item's last tile the same warps normalise O and store it.
+//               item's last tile the same warps normalise O: a full tile is
+//               staged in the freed stage of the item's last K (tile 0) or V
+//               (tile 1) tile for the store lane, the sequence's ragged last
+//               tile (and every tile in paged mode) is stored row by row.
 //   warp 8      MMA issuer (one thread): S_t = Q_t.K^T (M=128, N=128, K=16
 //               per instruction, 8 instructions), O_t += P_t.V (M=128,
 //               N=128, 8 instructions) with P_t read from TMEM; each group
 //               ends with tcgen05.commit on an mbarrier.
 //   warp 9      TMA producer: lane 0 takes the work items and loads both Q
-//               tiles and the K tiles (2-stage ring), lane 1 the V tiles.
+//               tiles and the K tiles (2-stage ring), lane 1 the V tiles;
+//               lane 2 (store lane, not in paged mode) writes the staged
+//               output tiles with TMA stores and returns their stages.
 // Every CTA builds the same work list in shared memory: only the non-empty
 // items, sequence-major (longest sequence first), heaviest tile first within
 // a sequence; items are taken from a global counter (dynamic balance) or,
