@@ -15,14 +15,18 @@
 // with rotate_half(y) = cat(-y[64:], y[:64]).  The cos/sin rows are the ones
 // the reference's RotaryEmbedding gathered (fp32, (B, S, D)).
 //
-// One warp per 8 (token, head) rows of one token, lane l holding elements
-// 4l..4l+3 of each; the RoPE partner of lane l is lane l ^ 16.  A warp issues
-// its 8 row loads and the token's cos/sin row before any math.  Rows of a
+// One warp per 8 (token, head) rows of one token.  With 16-byte aligned rows
+// a half-warp holds a row, lane l of it elements 8l..8l+7, and a pass covers
+// two rows; otherwise a warp holds a row, lane l elements 4l..4l+3.  The RoPE
+// partner of a lane is the lane half a row away (l ^ 8, or l ^ 16).  A warp
+// issues its 8 row loads and the token's cos/sin row before any math.  Rows of a
 // token: the q heads, then the k heads, then (when a pool is given) the v
 // heads.  A k row goes to k_out (optional) and to the pool slot of its
 // position; a v row only to the pool.  Pool addressing is the rows mode of the KV write: position =
 // seq_lens[row_ids[b]] + s.  Every index is range-checked; a bad one sets a
 // dev_status bit and the row's pool write is skipped.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
@@ -59,21 +63,12 @@ struct PrologueArgs {
   int32_t* dev_status;
 };
 
-B200_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
-B200_DEVICE void load4(const __nv_bfloat16* p, float (&x)[4]) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p);
-  x[0] = b200::bf16_lo(u.x);
-  x[1] = b200::bf16_hi(u.x);
-  x[2] = b200::bf16_lo(u.y);
-  x[3] = b200::bf16_hi(u.y);
-}
-
-B200_DEVICE void store4(__nv_bfloat16* p, const float (&x)[4]) {
-  uint2 u;
-  u.x = b200::pack_bf16x2(x[0], x[1]);
-  u.y = b200::pack_bf16x2(x[2], x[3]);
-  *reinterpret_cast<uint2*>(p) = u;
+// Round two floats to bf16 (nearest even) and back with one packed conversion:
+// the same values as rounding each alone, for half the conversions.
+B200_DEVICE void bf16_round2(float& a, float& b) {
+  const uint32_t u = b200::pack_bf16x2(a, b);
+  a = b200::bf16_lo(u);
+  b = b200::bf16_hi(u);
 }
 
 // Pool slot of token (b, s): writes the element offset of (phys, layer, h=0,
@@ -103,7 +98,17 @@ B200_DEVICE bool pool_slot(const PrologueArgs& a, int b, int s, int lane, int64_
   return true;
 }
 
+// VEC elements of a row per lane: 8 (a row per half-warp, two rows per pass,
+// 16-byte accesses; needs 16-byte aligned rows) or 4 (a row per warp, 8-byte
+// accesses).  With 8 the per-row work of a lane (addresses, the reduction,
+// the rsqrt, the weights) is spread over twice the elements.
+template <int VEC>
 __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
+  constexpr int kLanesPerRow = kD / VEC;        // 16 or 32
+  constexpr int kRowsPerPass = 32 / kLanesPerRow;
+  constexpr int kPasses = kRowsPerWarp / kRowsPerPass;
+  constexpr int kWords = VEC / 2;               // packed bf16 pairs per lane and row
+  using Vec = typename std::conditional<VEC == 8, uint4, uint2>::type;
   const int lane = threadIdx.x & 31;
   const int heads = a.num_heads + (a.k_pool != nullptr ? 2 : 1) * a.num_kv_heads;
   const int chunks = (heads + kRowsPerWarp - 1) / kRowsPerWarp;
@@ -114,15 +119,17 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
   const int64_t tok = gw / chunks;
   const int s = static_cast<int>(tok % a.n_tokens);
   const int b = static_cast<int>(tok / a.n_tokens);
-  const int d = 4 * lane;
+  const int sub = lane / kLanesPerRow;          // row of the pass this lane works on
+  const int li = lane % kLanesPerRow;
+  const int d = VEC * li;
   const int nrows = min(kRowsPerWarp, heads - h0);
 
   // every row load of this warp is issued before any math (memory-level parallelism)
-  uint2 raw[kRowsPerWarp];
+  Vec raw[kPasses];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    if (i < nrows) {
-      const int hh = h0 + i;
+  for (int i = 0; i < kPasses; ++i) {
+    const int hh = h0 + kRowsPerPass * i + sub;
+    if (hh - h0 < nrows) {
       const __nv_bfloat16* src;
       if (hh < a.num_heads) {
         src = a.q + b * a.q_b + hh * a.q_h + s * a.q_s;
@@ -131,13 +138,22 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
       } else {
         src = a.v + b * a.v_b + (hh - a.num_heads - a.num_kv_heads) * a.v_h + s * a.v_s;
       }
-      raw[i] = *reinterpret_cast<const uint2*>(src + d);
+      raw[i] = *reinterpret_cast<const Vec*>(src + d);
     }
   }
-  const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d);
-  const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d);
-  const float cf[4] = {bf16_round(c4.x), bf16_round(c4.y), bf16_round(c4.z), bf16_round(c4.w)};
-  const float sf[4] = {bf16_round(s4.x), bf16_round(s4.y), bf16_round(s4.z), bf16_round(s4.w)};
+  float cf[VEC], sf[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; e += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d + e);
+    const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d + e);
+    cf[e] = c4.x; cf[e + 1] = c4.y; cf[e + 2] = c4.z; cf[e + 3] = c4.w;
+    sf[e] = s4.x; sf[e + 1] = s4.y; sf[e + 2] = s4.z; sf[e + 3] = s4.w;
+  }
+#pragma unroll
+  for (int e = 0; e < VEC; e += 2) {
+    bf16_round2(cf[e], cf[e + 1]);
+    bf16_round2(sf[e], sf[e + 1]);
+  }
 
   int64_t k_off = 0, v_off = 0;
   const bool kv_rows = h0 + nrows > a.num_heads;
@@ -145,43 +161,68 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
       kv_rows && a.k_pool != nullptr && pool_slot(a, b, s, lane, &k_off, &v_off);
 
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    if (i >= nrows) break;
-    const int hh = h0 + i;
+  for (int i = 0; i < kPasses; ++i) {
+    if (kRowsPerPass * i >= nrows) break;
+    const int hh = h0 + kRowsPerPass * i + sub;
+    const bool live = hh - h0 < nrows;  // the pass's second row may lie past the chunk
     const bool is_q = hh < a.num_heads;
     const bool is_k = !is_q && hh < a.num_heads + a.num_kv_heads;
-    if (!is_q && !is_k) {  // v row: a plain copy into the pool
-      if (write_pool)
-        *reinterpret_cast<uint2*>(a.v_pool + v_off +
-                                  (hh - a.num_heads - a.num_kv_heads) * a.vp_h + d) = raw[i];
-      continue;
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[i]);
+    // the reduction and the RoPE exchange are shuffles over the whole warp,
+    // so every lane takes part; v rows and dead rows contribute zeros
+    float x[VEC];
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+      x[2 * w] = b200::bf16_lo(rw[w]);
+      x[2 * w + 1] = b200::bf16_hi(rw[w]);
     }
-    const float x[4] = {b200::bf16_lo(raw[i].x), b200::bf16_hi(raw[i].x), b200::bf16_lo(raw[i].y),
-                        b200::bf16_hi(raw[i].y)};
+    const bool norm = live && (is_q || is_k);
     // RMSNorm in fp32: mean of squares over the 128 elements of the row
-    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    float ss = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    for (int e = 0; e < VEC; ++e) ss = fmaf(x[e], x[e], ss);
+    if (!norm) ss = 0.f;
+#pragma unroll
+    for (int o = kLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float rms = __frsqrt_rn(ss / static_cast<float>(kD) + a.eps);
-    float w[4];
-    load4((is_q ? a.q_w : a.k_w) + d, w);
-    float y[4];
+    const __nv_bfloat16* wp = (is_q ? a.q_w : a.k_w) + d;
+    Vec wv = *reinterpret_cast<const Vec*>(wp);
+    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+    float y[VEC];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) y[e] = bf16_round((x[e] * rms) * w[e]);
-    // RoPE: partner elements d +- 64 live in lane ^ 16
-    float r[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float p = __shfl_xor_sync(0xffffffffu, y[e], 16);
-      const float rot = lane < 16 ? -p : p;
-      r[e] = bf16_round(bf16_round(y[e] * cf[e]) + bf16_round(rot * sf[e]));
+    for (int w = 0; w < kWords; ++w) {
+      y[2 * w] = (x[2 * w] * rms) * b200::bf16_lo(ww[w]);
+      y[2 * w + 1] = (x[2 * w + 1] * rms) * b200::bf16_hi(ww[w]);
+      bf16_round2(y[2 * w], y[2 * w + 1]);
     }
+    // RoPE: partner elements d +- 64 live in lane ^ (lanes per row / 2)
+    float yc[VEC], rs[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float p = __shfl_xor_sync(0xffffffffu, y[e], kLanesPerRow / 2);
+      const float rot = li < kLanesPerRow / 2 ? -p : p;
+      yc[e] = y[e] * cf[e];
+      rs[e] = rot * sf[e];
+    }
+    uint32_t packed[kWords];
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+      bf16_round2(yc[2 * w], yc[2 * w + 1]);
+      bf16_round2(rs[2 * w], rs[2 * w + 1]);
+      packed[w] = b200::pack_bf16x2(yc[2 * w] + rs[2 * w], yc[2 * w + 1] + rs[2 * w + 1]);
+    }
+    const Vec out = *reinterpret_cast<const Vec*>(packed);
+    if (!live) continue;
     if (is_q) {
-      store4(a.q_out + b * a.qo_b + hh * a.qo_h + s * a.qo_s + d, r);
-    } else {
+      *reinterpret_cast<Vec*>(a.q_out + b * a.qo_b + hh * a.qo_h + s * a.qo_s + d) = out;
+    } else if (is_k) {
       const int h = hh - a.num_heads;
-      if (a.k_out != nullptr) store4(a.k_out + b * a.ko_b + h * a.ko_h + s * a.ko_s + d, r);
-      if (write_pool) store4(a.k_pool + k_off + h * a.kp_h + d, r);
+      if (a.k_out != nullptr)
+        *reinterpret_cast<Vec*>(a.k_out + b * a.ko_b + h * a.ko_h + s * a.ko_s + d) = out;
+      if (write_pool) *reinterpret_cast<Vec*>(a.k_pool + k_off + h * a.kp_h + d) = out;
+    } else if (write_pool) {  // v row: a plain copy into the pool
+      *reinterpret_cast<Vec*>(a.v_pool + v_off + (hh - a.num_heads - a.num_kv_heads) * a.vp_h +
+                              d) = raw[i];
     }
   }
 }
@@ -300,7 +341,24 @@ extern "C" int b200_qk_norm_rope_kv_write(
   a.max_requests = max_requests;
   a.layer = layer;
   a.dev_status = dev_status;
-  qk_norm_rope_kv_write_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(a);
+  // 16-byte row pieces when every row and the weights allow them
+  bool v16 = b200host::aligned16(q) && b200host::aligned16(k) && b200host::aligned16(q_weight) &&
+             b200host::aligned16(k_weight) && b200host::aligned16(q_out);
+  for (int64_t st : strides) v16 = v16 && mult8(st);
+  if (k_out != nullptr)
+    v16 = v16 && b200host::aligned16(k_out) && mult8(ko_stride_b) && mult8(ko_stride_h) &&
+          mult8(ko_stride_s);
+  if (pool) {
+    v16 = v16 && b200host::aligned16(v) && mult8(v_stride_b) && mult8(v_stride_h) &&
+          mult8(v_stride_s) && mult8(kp_stride_blk) && mult8(kp_stride_layer) &&
+          mult8(kp_stride_h) && mult8(kp_stride_slot) && mult8(vp_stride_blk) &&
+          mult8(vp_stride_layer) && mult8(vp_stride_h) && mult8(vp_stride_slot);
+  }
+  if (v16)
+    qk_norm_rope_kv_write_kernel<8><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                      static_cast<cudaStream_t>(stream)>>>(a);
+  else
+    qk_norm_rope_kv_write_kernel<4><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                      static_cast<cudaStream_t>(stream)>>>(a);
   return b200host::status_from_cuda(cudaGetLastError());
 }
