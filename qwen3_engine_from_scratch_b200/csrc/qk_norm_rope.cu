@@ -167,6 +167,13 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
     const bool live = hh - h0 < nrows;  // the pass's second row may lie past the chunk
     const bool is_q = hh < a.num_heads;
     const bool is_k = !is_q && hh < a.num_heads + a.num_kv_heads;
+    if (h0 + kRowsPerPass * i >= a.num_heads + a.num_kv_heads) {
+      // every row of this pass is a v row (the same for the whole warp): a copy
+      if (live && write_pool)
+        *reinterpret_cast<Vec*>(a.v_pool + v_off + (hh - a.num_heads - a.num_kv_heads) * a.vp_h +
+                                d) = raw[i];
+      continue;
+    }
     const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[i]);
     // the reduction and the RoPE exchange are shuffles over the whole warp,
     // so every lane takes part; v rows and dead rows contribute zeros
