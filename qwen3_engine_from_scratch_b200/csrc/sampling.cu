@@ -207,14 +207,29 @@ B200_DEVICE int block_exclusive(int v, int* red, int* total) {
 // keys (bf16 scores: 16), so equal top bits mean equal keys.
 template <int NT, int PER>
 B200_DEVICE uint32_t kth_key(const uint32_t (&key)[PER], int k, int low, int* red) {
+  // red holds 2 x NT/32 partial sums: step i writes half i & 1, so one barrier
+  // per step suffices (a thread reads half i & 1 before it reaches the barrier
+  // of step i + 1, and half i & 1 is written again only in step i + 2)
+  uint32_t sk[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) sk[i] = key[i] >> low;
+  const int lane = threadIdx.x & 31;
   uint32_t t = 0;
+  int half = 0;
   for (int b = 31 - low; b >= 0; --b) {
     const uint32_t cand = t | (1u << b);
     int c = 0;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) c += (key[i] >> low) >= cand ? 1 : 0;
-    if (block_sum<NT>(c, red) >= k) t = cand;
+    for (int i = 0; i < PER; ++i) c += sk[i] >= cand ? 1 : 0;
+    c = __reduce_add_sync(0xffffffffu, c);
+    int* r = red + half * (NT / 32);
+    if (lane == 0) r[threadIdx.x >> 5] = c;
+    __syncthreads();
+    const int total = __reduce_add_sync(0xffffffffu, lane < NT / 32 ? r[lane] : 0);
+    if (total >= k) t = cand;
+    half ^= 1;
   }
+  __syncthreads();  // every partial read before red is reused
   return t;
 }
 
@@ -332,7 +347,7 @@ constexpr int kChunkPer = kChunk / kChunkThreads;  // 16 logits per thread
 __global__ void __launch_bounds__(kChunkThreads) sample_chunk_kernel(const SampleArgs a) {
   __shared__ __align__(16) uint64_t c[kMaxK];
   __shared__ uint64_t red64[kChunkThreads / 32];
-  __shared__ int red[kChunkThreads / 32];
+  __shared__ int red[2 * kChunkThreads / 32];
   __shared__ int s_count;
   const int chunk = blockIdx.x, row = blockIdx.y, tid = threadIdx.x;
   int k_sel;
@@ -418,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) sample_row_kernel(const SampleArgs a
   __shared__ __align__(16) uint64_t cand[kMaxK];   // (key << 32) | (~index): sorted descending
   __shared__ float prob[kMaxK];
   __shared__ uint64_t red64[kThreads / 32];
-  __shared__ int red[kThreads / 32];
+  __shared__ int red[2 * kThreads / 32];
   __shared__ ArgMax redm[32];
   __shared__ int s_count;
   const int row = blockIdx.x, tid = threadIdx.x;
