@@ -845,18 +845,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // instruction queue that the other tile's softmax and the MMA thread
         // use carries a quarter of the requests of row-per-thread stores)
         const float inv = 1.f / l;
+        const uint64_t inv2 = b200::f2_pack(inv, inv);
+        auto norm2 = [&](int e) {  // O / l of columns e, e + 1 (one packed multiply) as bf16
+          float lo, hi;
+          b200::f2_unpack(b200::f2_mul(b200::f2_pack(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])),
+                                       inv2),
+                          lo, hi);
+          return b200::pack_bf16x2(lo, hi);
+        };
 #pragma unroll
         for (int c = 0; c < kD / 8; ++c) {
           const int e = 8 * c;
           b200::st_shared_v4(stage + (c >> 3) * kKVBlock + r * 128 + (((c & 7) ^ (r & 7)) << 4),
-                             b200::pack_bf16x2(__uint_as_float(ov[e]) * inv,
-                                               __uint_as_float(ov[e + 1]) * inv),
-                             b200::pack_bf16x2(__uint_as_float(ov[e + 2]) * inv,
-                                               __uint_as_float(ov[e + 3]) * inv),
-                             b200::pack_bf16x2(__uint_as_float(ov[e + 4]) * inv,
-                                               __uint_as_float(ov[e + 5]) * inv),
-                             b200::pack_bf16x2(__uint_as_float(ov[e + 6]) * inv,
-                                               __uint_as_float(ov[e + 7]) * inv));
+                             norm2(e), norm2(e + 2), norm2(e + 4), norm2(e + 6));
         }
         b200::fence_proxy_async_smem();  // the rows, then the store lane's TMA stores
         mbar_arrive(bar_st(t, n));
