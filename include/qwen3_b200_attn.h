@@ -113,6 +113,31 @@ int b200_kv_scatter_slots(const void* k, const void* v,
                           int num_blocks, int layer, int32_t* dev_status, void* stream);
 
 /*
+ * KV-cache write of one request from a host position: replaces the body of
+ * PagedKVCache.update (qwen3/PagedKVcache.py:187-214), whose write position is
+ * the handle's host-side seq_len.  Token s (0 <= s < n_tokens), head h:
+ *     pos  = start_pos + s;  page = pos / 16;  (page < num_pages, else flagged
+ *            B200_DEV_SEQ_OVERFLOW and skipped, where the reference's
+ *            block_table_tensor[:num_pages][page] would raise)
+ *     phys = block_table_row[page];  off = pos % 16;
+ *     k_pool[phys, layer, h, off, :] = k_new[h, s, :]   (same for v)
+ * block_table_row: the handle's row of the 2-D block table (num_pages entries
+ * allocated); k_new/v_new (num_kv_heads, n_tokens, head_dim) with strides
+ * (head, token), head_dim stride 1.  Pool strides as b200_kv_scatter_rows.
+ */
+int b200_kv_scatter_span(const void* k_new, const void* v_new,
+                         int64_t kn_stride_h, int64_t kn_stride_s,
+                         int64_t vn_stride_h, int64_t vn_stride_s,
+                         void* k_pool, void* v_pool,
+                         int64_t kp_stride_blk, int64_t kp_stride_layer,
+                         int64_t kp_stride_h, int64_t kp_stride_slot,
+                         int64_t vp_stride_blk, int64_t vp_stride_layer,
+                         int64_t vp_stride_h, int64_t vp_stride_slot,
+                         const int32_t* block_table_row, int num_pages, int start_pos,
+                         int n_tokens, int num_kv_heads, int head_dim, int block_size,
+                         int num_blocks, int layer, int32_t* dev_status, void* stream);
+
+/*
  * Split-K paged decode: workspace bytes needed for `batch` requests, `num_heads`
  * query heads and a block table `max_pages` wide, with `pages_per_split`
  * pages per split.  <= 0 returns enough for any split the library may pick by
@@ -194,13 +219,20 @@ int b200_paged_decode_kv_write(const void* q, int64_t q_stride_b, int64_t q_stri
  * pool and run a fixed arena, FFI bindings holding raw device pointers but no
  * device allocator, loops that must not pay cudaMalloc's latency or its
  * implicit synchronisation.  Same arguments and results as b200_paged_decode
- * minus the workspace: the split partials live in a file-scope device array of
- * B200_DECODE_NOALLOC_SCRATCH_BYTES per GPU (held until process exit).
- * Returns B200_ERR_WORKSPACE when b200_paged_decode_workspace_size(...) for
- * these shapes exceeds that maximum.  Calls no allocator.  The first call on a
- * device looks up the array's device address; make it before any stream
- * capture on that device.  All calls on a device share the array: calls whose
- * kernels overlap on the GPU (unordered streams) race and must not be issued.
+ * minus the workspace: the split workspace lives in a file-scope device array
+ * of B200_DECODE_NOALLOC_SCRATCH_BYTES per GPU (held until process exit).
+ * Returns B200_ERR_WORKSPACE when b200_paged_decode_workspace_size(batch,
+ * num_heads, max_pages, s) exceeds that maximum, s being the split the call
+ * uses: pages_per_split if > 0, else b200_paged_decode_default_split(batch,
+ * num_kv_heads, max_pages) -- not the worst-case figure that
+ * workspace_size(..., 0) reports, which can refuse shapes this entry accepts.
+ * Calls no allocator.  The array starts with the split-arrival counters, which
+ * must be zero at launch: every call clears those of its own pairs with one
+ * cudaMemsetAsync on `stream` before the kernel.  The first call in a CUDA
+ * context looks up the array's device address (cached per device and context
+ * id); make it before any stream capture on that device, and again after a
+ * device reset.  All calls on a device share the array: calls whose kernels
+ * overlap on the GPU (unordered streams) race and must not be issued.
  */
 #define B200_DECODE_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 int b200_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,

@@ -27,6 +27,8 @@ from .ops import (  # noqa: F401
     paged_decode_kv_write,
     kv_scatter_rows,
     kv_scatter_slots,
+    kv_scatter_span,
+    paged_cache_update,
     qk_norm_rope_kv_write,
     paged_prefill,
     sample_tokens,

@@ -57,6 +57,9 @@ SIGNATURES = {
     "b200_kv_scatter_slots": (_I, [_P, _P, _I64, _I64, _I64, _I64,
                                    _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                    _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "b200_kv_scatter_span": (_I, [_P, _P, _I64, _I64, _I64, _I64,
+                                  _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                  _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "b200_paged_decode_workspace_size": (_SZ, [_I, _I, _I, _I]),
     "b200_paged_decode_default_split": (_I, [_I, _I, _I]),
     "b200_paged_decode": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64,

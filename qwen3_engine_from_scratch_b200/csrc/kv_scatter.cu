@@ -6,6 +6,10 @@
 //   rows  mode: position = seq_lens[row_ids[b]] + s, page from the 2-D block
 //               table (update_kv_batch_kernel, qwen3/kernels/paged_attention.py:
 //               292-350, and PagedKVCache.update, qwen3/PagedKVcache.py:187-214)
+//   span  mode: one request, position = start_pos + s with start_pos from the
+//               host (PagedKVCache.update exactly: its write position is the
+//               handle's host seq_len, qwen3/PagedKVcache.py:189-203), page from
+//               one block-table row of num_pages allocated entries
 //   slots mode: slot = slot_mapping[t] = phys * block_size + offset
 //
 // Every index is range-checked; an out-of-range index sets a dev_status bit
@@ -35,7 +39,8 @@ struct RowsArgs {
   const int32_t* seq_lens;
   const int32_t* block_table;
   int64_t bt_row;
-  const int32_t* row_ids;
+  const int32_t* row_ids;  // nullptr: span mode (row 0 of block_table, position start_pos + s)
+  int64_t start_pos;
   int batch, n_tokens, num_kv_heads, block_size, num_blocks, max_pages, max_requests, layer;
   int32_t* dev_status;
 };
@@ -51,12 +56,18 @@ __global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArg
   const int s = static_cast<int>(r % a.n_tokens);
   const int b = static_cast<int>(r / a.n_tokens);
 
-  const int row = a.row_ids[b];
-  if (row < 0 || row >= a.max_requests) {
-    if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_ROW);
-    return;
+  int row = 0;
+  int64_t pos;
+  if (a.row_ids != nullptr) {
+    row = a.row_ids[b];
+    if (row < 0 || row >= a.max_requests) {
+      if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_ROW);
+      return;
+    }
+    pos = static_cast<int64_t>(a.seq_lens[row]) + s;
+  } else {
+    pos = a.start_pos + s;
   }
-  const int64_t pos = static_cast<int64_t>(a.seq_lens[row]) + s;
   const int64_t page = pos / a.block_size;
   if (pos < 0 || page >= a.max_pages) {
     if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
@@ -159,6 +170,7 @@ extern "C" int b200_kv_scatter_rows(
   a.vp_slot = vp_stride_slot;
   a.seq_lens = seq_lens; a.block_table = block_table; a.bt_row = bt_stride_row;
   a.row_ids = row_ids;
+  a.start_pos = 0;
   a.batch = batch; a.n_tokens = n_tokens; a.num_kv_heads = num_kv_heads;
   a.block_size = block_size; a.num_blocks = num_blocks; a.max_pages = max_pages;
   a.max_requests = max_requests; a.layer = layer; a.dev_status = dev_status;
@@ -211,5 +223,54 @@ extern "C" int b200_kv_scatter_slots(
   if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
   kv_scatter_slots_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
                             static_cast<cudaStream_t>(stream)>>>(a);
+  return b200host::status_from_cuda(cudaGetLastError());
+}
+
+extern "C" int b200_kv_scatter_span(
+    const void* k_new, const void* v_new, int64_t kn_stride_h, int64_t kn_stride_s,
+    int64_t vn_stride_h, int64_t vn_stride_s, void* k_pool, void* v_pool, int64_t kp_stride_blk,
+    int64_t kp_stride_layer, int64_t kp_stride_h, int64_t kp_stride_slot, int64_t vp_stride_blk,
+    int64_t vp_stride_layer, int64_t vp_stride_h, int64_t vp_stride_slot,
+    const int32_t* block_table_row, int num_pages, int start_pos, int n_tokens, int num_kv_heads,
+    int head_dim, int block_size, int num_blocks, int layer, int32_t* dev_status, void* stream) {
+  if (n_tokens < 0 || num_pages < 0 || start_pos < 0 || num_kv_heads <= 0 || block_size <= 0 ||
+      num_blocks <= 0 || layer < 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (n_tokens == 0) return B200_OK;
+  if (!k_new || !v_new || !k_pool || !v_pool || !block_table_row || num_pages == 0)
+    return B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return B200_ERR_UNSUPPORTED;
+  if (!b200host::aligned16(k_new) || !b200host::aligned16(v_new) ||
+      !b200host::aligned16(k_pool) || !b200host::aligned16(v_pool))
+    return B200_ERR_ALIGNMENT;
+  const int64_t strides[] = {kn_stride_h, kn_stride_s, vn_stride_h, vn_stride_s,
+                             kp_stride_blk, kp_stride_layer, kp_stride_h, kp_stride_slot,
+                             vp_stride_blk, vp_stride_layer, vp_stride_h, vp_stride_slot};
+  for (int64_t s : strides)
+    if (!mult8(s)) return B200_ERR_ALIGNMENT;
+
+  RowsArgs a;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.kn_b = 0; a.kn_h = kn_stride_h; a.kn_s = kn_stride_s;
+  a.vn_b = 0; a.vn_h = vn_stride_h; a.vn_s = vn_stride_s;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.kp_blk = kp_stride_blk; a.kp_layer = kp_stride_layer; a.kp_h = kp_stride_h;
+  a.kp_slot = kp_stride_slot;
+  a.vp_blk = vp_stride_blk; a.vp_layer = vp_stride_layer; a.vp_h = vp_stride_h;
+  a.vp_slot = vp_stride_slot;
+  a.seq_lens = nullptr; a.block_table = block_table_row; a.bt_row = 0;
+  a.row_ids = nullptr;
+  a.start_pos = start_pos;
+  a.batch = 1; a.n_tokens = n_tokens; a.num_kv_heads = num_kv_heads;
+  a.block_size = block_size; a.num_blocks = num_blocks; a.max_pages = num_pages;
+  a.max_requests = 1; a.layer = layer; a.dev_status = dev_status;
+
+  const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kChunksPerRow;
+  const int64_t blocks = (threads + kThreads - 1) / kThreads;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  kv_scatter_rows_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
+                           static_cast<cudaStream_t>(stream)>>>(a);
   return b200host::status_from_cuda(cudaGetLastError());
 }

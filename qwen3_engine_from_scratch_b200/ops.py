@@ -16,6 +16,8 @@ this module                                 reference (uphome/Qwen3-engine-from-
 ``kv_scatter_rows``                         PagedKVCache.update (qwen3/PagedKVcache.py:177-214)
                                             for a whole batch, one launch
 ``kv_scatter_slots``                        vLLM-style slot_mapping write (new entry point)
+``kv_scatter_span``                         the write of PagedKVCache.update
+                                            (qwen3/PagedKVcache.py:187-214), host position
 ==========================================  ==================================================
 
 The ``triton_*`` names are kept only so existing call sites bind unchanged; no
@@ -46,6 +48,8 @@ __all__ = [
     "paged_decode_kv_write",
     "kv_scatter_rows",
     "kv_scatter_slots",
+    "kv_scatter_span",
+    "paged_cache_update",
     "qk_norm_rope_kv_write",
     "paged_prefill",
     "sample_tokens",
@@ -174,6 +178,63 @@ def kv_scatter_rows(k_new, v_new, k_buffer, v_buffer, seq_lens, block_table_2d, 
         B, S, Hkv, D, bs, nb, block_table_2d.shape[1], block_table_2d.shape[0], int(layer_idx),
         _status_ptr(k_buffer.device), _stream())
     _native.check(st, "b200_kv_scatter_rows")
+
+
+def kv_scatter_span(k_new, v_new, k_buffer, v_buffer, block_table_row, num_pages, start_pos,
+                    layer_idx):
+    """Write one request's S tokens from the host position ``start_pos``.
+
+    The byte movement of PagedKVCache.update (qwen3/PagedKVcache.py:198-214):
+    token s lands at position ``start_pos + s`` through ``block_table_row``
+    (the handle's row of the 2-D block table, ``num_pages`` entries allocated).
+    k_new, v_new: (Hkv, S, D) bf16, any strides with a contiguous head_dim.
+    A position past ``num_pages`` pages is flagged in the device status and
+    skipped (the reference's indexing would raise).  One launch.
+    """
+    assert k_new.dim() == 3 and k_new.shape == v_new.shape, "k_new/v_new must be (Hkv, S, D)"
+    assert k_new.dtype == torch.bfloat16 and v_new.dtype == torch.bfloat16, "bf16 only"
+    _check_pool(k_buffer, v_buffer)
+    assert block_table_row.dtype == torch.int32 and block_table_row.is_cuda, \
+        "block_table_row must be an int32 GPU tensor"
+    assert block_table_row.dim() == 1 and block_table_row.stride(0) == 1, \
+        "block_table_row must be one contiguous row of the block table"
+    Hkv, S, D = k_new.shape
+    nb, nl, hkv_p, bs, d_p = k_buffer.shape
+    assert Hkv == hkv_p and D == d_p, "k_new heads/head_dim do not match the pool"
+    assert 0 <= int(num_pages) <= block_table_row.numel(), "num_pages outside the block-table row"
+    k_new = _vec_ready(k_new, 0, 1)
+    v_new = _vec_ready(v_new, 0, 1)
+    st = _native.load().b200_kv_scatter_span(
+        k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        v_new.stride(0), v_new.stride(1), k_buffer.data_ptr(), v_buffer.data_ptr(),
+        k_buffer.stride(0), k_buffer.stride(1), k_buffer.stride(2), k_buffer.stride(3),
+        v_buffer.stride(0), v_buffer.stride(1), v_buffer.stride(2), v_buffer.stride(3),
+        block_table_row.data_ptr(), int(num_pages), int(start_pos), S, Hkv, D, bs, nb,
+        int(layer_idx), _status_ptr(k_buffer.device), _stream())
+    _native.check(st, "b200_kv_scatter_span")
+
+
+def paged_cache_update(cache, layer_idx, k_new, v_new):
+    """``PagedKVCache.update`` (qwen3/PagedKVcache.py:177-214) on the scatter kernel.
+
+    ``cache`` is a request handle with the reference's attributes (``_pool``,
+    ``seq_len``, ``block_table``, ``num_pages``, ``block_table_tensor``,
+    ``_allocate_block``): the reference's own class or this package's mirror.
+    Same steps as the reference: pages for ``ceil((seq_len + S_new) / 16)``
+    positions are allocated first (host bookkeeping, :193-195), then request
+    0's S_new tokens are written from position ``seq_len`` (:198-214) -- in one
+    launch instead of two torch ``index_put`` plus their index arithmetic.
+    k_new, v_new: (B, Hkv, S_new, D) bf16 on the GPU; as in the reference only
+    ``k_new[0]`` / ``v_new[0]`` are written.  ``seq_len`` is not advanced.
+    """
+    pool = cache._pool
+    S_new = k_new.shape[2]
+    write_pos = int(cache.seq_len)
+    need_blocks = (write_pos + S_new + pool.block_size - 1) // pool.block_size
+    while len(cache.block_table) < need_blocks:
+        cache._allocate_block()
+    kv_scatter_span(k_new[0], v_new[0], pool.k_buffer, pool.v_buffer, cache.block_table_tensor,
+                    cache.num_pages, write_pos, layer_idx)
 
 
 def update_kv_batch_triton(k_new, v_new, k_buffer, v_buffer, seq_lens, block_table_2d, row_ids,
@@ -465,8 +526,10 @@ def triton_paged_attention_decode_batch(q, k_new, v_new, kv_caches, layer_idx, s
     int32 device tensor of block-table rows (None: reserve_next + build here,
     as the reference's test path does, :257-264).  Writes the new K/V at
     ``seq_lens[row]`` (the scatter) and then attends over ``seq_lens[row] + 1``
-    tokens.  Returns (B, 1, H*D).  ``scaling`` is applied to q.k (for Qwen3 it
-    equals the reference kernel's built-in 1/sqrt(head_dim)).
+    tokens.  Returns (B, 1, H*D).  Like the reference, ``scaling`` is accepted
+    and ignored: its Triton path always scales q.k by 1/sqrt(head_dim)
+    (qwen3/kernels/paged_attention.py:161), which for Qwen3 equals the
+    caller's ``head_dim ** -0.5``.
     """
     assert q.shape[2] == 1, "decode kernel supports S == 1 only"
     assert q.dtype == torch.bfloat16, "decode kernel supports bf16 only"
@@ -479,20 +542,26 @@ def triton_paged_attention_decode_batch(q, k_new, v_new, kv_caches, layer_idx, s
     pool = _pool_of(kv_caches[0])
     out = paged_decode_kv_write(q.squeeze(2), k_new.squeeze(2), v_new.squeeze(2),
                                 pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
-                                pool.block_table_2d, pool.seq_lens, row_ids, scaling)
+                                pool.block_table_2d, pool.seq_lens, row_ids,
+                                1.0 / math.sqrt(q.shape[3]))
     num_heads, head_dim = q.shape[1], q.shape[3]
     return out.reshape(B, 1, num_heads * head_dim)
 
 
 def triton_paged_attention_decode(q, k_new, v_new, kv_cache, layer_idx, scaling):
-    """Single-request decode (qwen3/kernels/paged_attention.py:181-219): B == 1."""
+    """Single-request decode (qwen3/kernels/paged_attention.py:181-219): B == 1.
+
+    ``scaling`` is accepted and ignored, as in the reference (its kernel entry
+    uses 1/sqrt(head_dim), qwen3/kernels/paged_attention.py:161).
+    """
     assert q.shape[2] == 1, "decode kernel supports S == 1 only"
     assert q.dtype == torch.bfloat16, "decode kernel supports bf16 only"
     row_ids = _row_ids_of(kv_cache, q.device)
     pool = _pool_of(kv_cache)
     out = paged_decode_kv_write(q.squeeze(2), k_new.squeeze(2), v_new.squeeze(2),
                                 pool.k_buffer[:, layer_idx], pool.v_buffer[:, layer_idx],
-                                pool.block_table_2d, pool.seq_lens, row_ids, scaling)
+                                pool.block_table_2d, pool.seq_lens, row_ids,
+                                1.0 / math.sqrt(q.shape[3]))
     B, num_heads, head_dim = q.shape[0], q.shape[1], q.shape[3]
     return out.reshape(B, 1, num_heads * head_dim)
 

@@ -148,14 +148,10 @@ class PagedKVCache:
         """Write S_new tokens from position seq_len (:177-214) with the scatter kernel.
 
         k_new, v_new: (1, Hkv, S_new, D).  Allocates pages first, like the
-        reference.  The kernel reads the start position from the device copy
-        ``pool.seq_lens[row_id]``, which advance_seq_len keeps equal to seq_len.
+        reference, then one launch writes request 0's tokens from the host
+        ``seq_len`` through this handle's block-table row.
         """
-        S_new = k_new.shape[2]
-        self._ensure_pages(self.seq_len + S_new)
-        row_ids = ops._row_ids_of(self, k_new.device)
-        ops.kv_scatter_rows(k_new, v_new, self._pool.k_buffer, self._pool.v_buffer,
-                            self._pool.seq_lens, self._pool.block_table_2d, row_ids, layer_idx)
+        ops.paged_cache_update(self, layer_idx, k_new, v_new)
 
     def advance_seq_len(self, n: int = 1):
         self.seq_len += n

@@ -11,7 +11,12 @@ import pytest
 import torch
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REFERENCE = os.environ.get("QWEN3_REFERENCE", "/root/reference")
+# checkout of the reference engine (its `qwen3` package), for the tests that bind
+# into its modules; they are skipped when QWEN3_REFERENCE is not set
+REFERENCE = os.environ.get("QWEN3_REFERENCE")
+needs_reference = pytest.mark.skipif(
+    not REFERENCE or not os.path.isdir(os.path.join(REFERENCE, "qwen3")),
+    reason="set QWEN3_REFERENCE to a checkout of the reference engine")
 
 
 def test_lpt_partition_balances_and_covers():
@@ -78,8 +83,7 @@ def test_gloo_world2_tp_gather_and_sharding():
     assert all(total == sum([300, 20, 4000, 128, 77, 1000]) for _, _, total in res)
 
 
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REFERENCE, "qwen3")),
-                    reason="reference checkout not present")
+@needs_reference
 def test_shim_binds_into_reference_modules(monkeypatch):
     monkeypatch.syspath_prepend(REFERENCE)
     import importlib
@@ -92,7 +96,9 @@ def test_shim_binds_into_reference_modules(monkeypatch):
         assert attn.triton_paged_attention_decode is ops.triton_paged_attention_decode
         assert attn.flash_attention_prefill_batched is ops.flash_attention_prefill_batched
         assert kvc.update_kv_batch_triton is ops.update_kv_batch_triton
-        assert len(bound) == 13
+        assert kvc.PagedKVCache.update is shim._paged_cache_update
+        assert "qwen3.PagedKVcache.PagedKVCache.update" in bound
+        assert len(bound) == 14
         assert importlib.import_module("qwen3.sampling").sample_tokens is ops.sample_tokens
         from qwen3_engine_from_scratch_b200 import graph_runner
         assert importlib.import_module("qwen3.graph_runner").GraphRunner is graph_runner.GraphRunner
@@ -100,6 +106,38 @@ def test_shim_binds_into_reference_modules(monkeypatch):
         shim.uninstall()
     attn = importlib.import_module("qwen3.attention")
     assert attn.triton_paged_attention_decode_batch is not ops.triton_paged_attention_decode_batch
+    assert importlib.import_module("qwen3.PagedKVcache").PagedKVCache.update is not \
+        shim._paged_cache_update
+
+
+@needs_reference
+def test_shim_cache_update_keeps_reference_cpu_path(monkeypatch):
+    """With the shim installed, the reference's PagedKVCache.update on CPU tensors
+    (outside the kernel's contract) still runs the reference's own method: the
+    block table and pool bytes equal an uninstalled run's."""
+    monkeypatch.syspath_prepend(REFERENCE)
+    import importlib
+    from qwen3_engine_from_scratch_b200 import shim
+    kvc = importlib.import_module("qwen3.PagedKVcache")
+
+    def run():
+        pool = kvc.KVCachePool(num_blocks=16, num_layers=2, block_size=16, num_kv_heads=2,
+                               head_dim=128, dtype=torch.float32, max_seq_len=128, max_requests=4)
+        c = kvc.PagedKVCache(pool)
+        g = torch.Generator().manual_seed(5)
+        c.update(1, torch.randn(1, 2, 21, 128, generator=g), torch.randn(1, 2, 21, 128, generator=g))
+        c.advance_seq_len(21)
+        c.update(1, torch.randn(1, 2, 15, 128, generator=g), torch.randn(1, 2, 15, 128, generator=g))
+        return pool.block_table_2d.clone(), pool.k_buffer.clone(), pool.v_buffer.clone()
+
+    want = run()
+    shim.install()
+    try:
+        assert kvc.PagedKVCache.update is shim._paged_cache_update
+        got = run()
+    finally:
+        shim.uninstall()
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
 
 
 def test_reference_signatures_match():
@@ -124,6 +162,7 @@ def test_reference_signatures_match():
         assert got[:len(params)] == params, (name, got)
 
 
+@needs_reference
 def test_graph_runner_signature_matches_reference(monkeypatch):
     """GraphRunner takes the reference's constructor and replay arguments."""
     import inspect
