@@ -27,8 +27,9 @@ Multi-GPU: one process per GPU (torchrun), each rank owns its own requests,
 pool and block table -- no collective on the data path ("scaling": "weak").
 The default line also carries a ``c4`` object: config 4 (Qwen3-8B heads 32/8,
 512 requests of log-uniform [256,32768] tokens) with the 512 requests sharded
-over the ranks by LPT on length ("scaling": "strong"), max-over-ranks time; and
-a ``prefill`` object (config 3 varlen prefill, with its own ``e2e``, ``clocks``
+over the ranks by LPT on length ("scaling": "strong"), max-over-ranks time; a
+``c5`` object (config 5: Qwen3-0.6B end to end, 256 requests decoded from CUDA
+graphs, data parallel over the ranks, tokens/s); and a ``prefill`` object (config 3 varlen prefill, with its own ``e2e``, ``clocks``
 and ``cpu_baseline``).  ``--config c4`` / ``--config c3`` make those the headline.
 
 ``--impl reference``: the reference's own algorithm (the CPU oracle port of
@@ -425,11 +426,17 @@ def run_b200(args, rank, world, local_rank):
     del layer_call, step, e2e_step, time_e2e
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
-    c4 = None
+    c4 = c5 = None
     if args.config == "c2" and not args.no_c4:
         # config 4 strong scaling, every rank (collectives inside)
         c4 = run_c4_leg(args, rank, world, local_rank, steps=max(5, min(args.steps, 20)),
                         warmup=3)
+    if args.config == "c2" and not args.no_c5:
+        # config 5 end to end, data parallel over the ranks (collectives inside)
+        try:
+            c5 = run_c5_leg(args, rank, world, local_rank)
+        except RuntimeError as e:
+            c5 = {"error": str(e)[:200]}
     if rank != 0:
         return None
 
@@ -499,6 +506,8 @@ def run_b200(args, rank, world, local_rank):
     }
     if c4 is not None:
         line["c4"] = c4
+    if c5 is not None:
+        line["c5"] = c5
     if not args.no_prefill:
         try:
             line["prefill"] = run_prefill(args, rank, world, local_rank, steps=30, warmup=5,
@@ -592,6 +601,62 @@ def run_c4_leg(args, rank, world, local_rank, steps, warmup):
                       "inputs larger than L2 (%.2f GB read per rank per step)" % (nbytes / 1e9),
             "limiter": "the slowest rank (LPT length imbalance and per-rank wave quantisation); "
                        "no collective on the path"}
+
+
+def run_c5_leg(args, rank, world, local_rank, new_tokens=256, requests=256):
+    """Config 5: Qwen3-0.6B end to end (28 layers, random N(0, 0.02) weights),
+    256 concurrent requests with prompts U[32, 1024] and 256 generated tokens
+    each: one prefill of every prompt, then decode steps of the whole batch
+    replayed from a CUDA graph (GraphRunner), greedy sampling with the fused
+    sampler.  Requests are sharded over the ranks (data parallel, LPT on prompt
+    length); tokens/s = all generated tokens / max-over-ranks device time."""
+    import torch
+    import torch.distributed as dist
+    from qwen3_engine_from_scratch_b200 import e2e_model
+    from qwen3_engine_from_scratch_b200.dist import lpt_partition
+
+    device = torch.device("cuda", local_rank)
+    cfg = e2e_model.QWEN3_0_6B
+    prompts = e2e_model.synthetic_prompts(requests, 32, 1024, cfg["vocab"], seed=55)
+    mine = lpt_partition([len(p) + new_tokens for p in prompts], world)[rank]
+    local = [prompts[i] for i in mine]
+    model = e2e_model.Qwen3DecodeModel(device, seed=5, **cfg)
+    # warm-up: a small serve of the same shapes compiles nothing but loads every kernel
+    e2e_model.serve(model, local[:4], 4, device, graph=True, buckets=(4,))
+    if world > 1:
+        dist.barrier()
+    tokens, st = e2e_model.serve(model, local, new_tokens, device, graph=True,
+                                 buckets=(len(local),))
+    t = torch.tensor([st["prefill_ms"] + st["decode_ms"], st["decode_ms"], st["prefill_ms"],
+                      float(len(local))], dtype=torch.float64, device=device)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        total_ms, dec_ms, pre_ms = float(tmax[0]), float(tmax[1]), float(tmax[2])
+    else:
+        total_ms, dec_ms, pre_ms = float(t[0]), float(t[1]), float(t[2])
+    del model
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    gen = requests * new_tokens
+    ok = bool((tokens >= 0).all() and (tokens < cfg["vocab"]).all())
+    return {"workload": "c5_qwen3_0.6b_end_to_end", "model": "Qwen3-0.6B shape, random N(0,0.02)",
+            "layers": cfg["layers"], "requests": requests, "prompts": "U[32,1024]",
+            "new_tokens_per_request": new_tokens, "parallelism": f"data parallel x{world}",
+            "requests_per_rank_max": int(max(len(s) for s in lpt_partition(
+                [len(p) + new_tokens for p in prompts], world))),
+            "tok_per_s": round(gen / (total_ms / 1e3), 1),
+            "tok_per_s_per_gpu": round(gen / (total_ms / 1e3) / world, 1),
+            "decode_tok_per_s": round(requests * (new_tokens - 1) / (dec_ms / 1e3), 1),
+            "ms_total": round(total_ms, 2), "ms_prefill": round(pre_ms, 2),
+            "ms_decode": round(dec_ms, 2), "decode_steps": new_tokens - 1,
+            "tokens_in_vocab": ok,
+            "timing": "CUDA events around the prefill of all prompts and the decode loop "
+                      "(graph replays + fused greedy sampler, host page reservation between "
+                      "steps), max over ranks",
+            "path": "prologue qk_norm_rope_kv_write, varlen prefill, kv_scatter_slots, fused "
+                    "KV-write decode via triton_paged_attention_decode_batch, sample_tokens; "
+                    "GEMMs / MLP / norms in torch"}
 
 
 def bench_sampling(device, steps=20, warmup=3):
@@ -1124,6 +1189,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-c4", action="store_true",
                     help="skip the config-4 strong-scaling leg of the default run")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="skip the config-5 end-to-end leg of the default run")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers per step (default: 28 for c2); 1 gives a small case for profiling")
     args = ap.parse_args()
