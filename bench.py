@@ -699,7 +699,7 @@ def bench_sampling(device, steps=20, warmup=3):
              "torch_topk_only": lambda: torch.topk(logits, 50, dim=-1, largest=True, sorted=True),
              "greedy": lambda: ops.sample_tokens(logits, 0.0),
              "torch_argmax": lambda: logits.argmax(dim=-1)}
-    res = {"kernel": "sample_chunk_kernel + sample_row_kernel", "batch": B, "vocab": V,
+    res = {"kernel": "sample_chunk_kernel + sample_row_fast_kernel", "batch": B, "vocab": V,
            "dtype": "bf16", "params": "temperature 0.7, top_k 50, top_p 0.9",
            "timing": "per call from Python (eager, host included) and device time of the "
                      "call replayed from a CUDA graph"}

@@ -60,16 +60,9 @@ struct PrologueArgs {
   const int32_t* row_ids;
   int batch, n_tokens, num_heads, num_kv_heads, block_size, num_blocks, max_pages, max_requests,
       layer;
+  int total_warps;  // batch * n_tokens * row chunks (below 2^31)
   int32_t* dev_status;
 };
-
-// Round two floats to bf16 (nearest even) and back with one packed conversion:
-// the same values as rounding each alone, for half the conversions.
-B200_DEVICE void bf16_round2(float& a, float& b) {
-  const uint32_t u = b200::pack_bf16x2(a, b);
-  a = b200::bf16_lo(u);
-  b = b200::bf16_hi(u);
-}
 
 // Pool slot of token (b, s): writes the element offset of (phys, layer, h=0,
 // off) into *k_off / *v_off; false (and a status bit from lane 0) if an index
@@ -98,10 +91,31 @@ B200_DEVICE bool pool_slot(const PrologueArgs& a, int b, int s, int lane, int64_
   return true;
 }
 
+// Packed bf16 pair arithmetic (one rounding of the exact result, as the
+// reference's bf16 tensor ops round their fp32 result: for bf16 operands the
+// fp32 product is exact, and an fp32 sum is either exact or rounds to the
+// same bf16 value as the exact sum).
+B200_DEVICE uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+B200_DEVICE uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// fp32 pair of the two bf16 halves of w
+B200_DEVICE uint64_t bf2_to_f2(uint32_t w) {
+  return b200::f2_pack(b200::bf16_lo(w), b200::bf16_hi(w));
+}
+
 // VEC elements of a row per lane: 8 (a row per half-warp, two rows per pass,
 // 16-byte accesses; needs 16-byte aligned rows) or 4 (a row per warp, 8-byte
 // accesses).  With 8 the per-row work of a lane (addresses, the reduction,
-// the rsqrt, the weights) is spread over twice the elements.
+// the rsqrt, the weights) is spread over twice the elements.  After the
+// normalisation every value is a packed bf16 pair: the RoPE partner is
+// exchanged as pairs and the products and the sum are packed bf16 operations.
 template <int VEC>
 __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
   constexpr int kLanesPerRow = kD / VEC;        // 16 or 32
@@ -112,13 +126,13 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
   const int lane = threadIdx.x & 31;
   const int heads = a.num_heads + (a.k_pool != nullptr ? 2 : 1) * a.num_kv_heads;
   const int chunks = (heads + kRowsPerWarp - 1) / kRowsPerWarp;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-  const int64_t total = static_cast<int64_t>(a.batch) * a.n_tokens * chunks;
-  if (gw >= total) return;
-  const int h0 = static_cast<int>(gw % chunks) * kRowsPerWarp;
-  const int64_t tok = gw / chunks;
-  const int s = static_cast<int>(tok % a.n_tokens);
-  const int b = static_cast<int>(tok / a.n_tokens);
+  // the host keeps the warp count below 2^31: 32-bit index arithmetic
+  const int gw = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  if (gw >= a.total_warps) return;
+  const int tok = gw / chunks;
+  const int h0 = (gw - tok * chunks) * kRowsPerWarp;
+  const int b = tok / a.n_tokens;
+  const int s = tok - b * a.n_tokens;
   const int sub = lane / kLanesPerRow;          // row of the pass this lane works on
   const int li = lane % kLanesPerRow;
   const int d = VEC * li;
@@ -141,19 +155,19 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
       raw[i] = *reinterpret_cast<const Vec*>(src + d);
     }
   }
-  float cf[VEC], sf[VEC];
+  // cos / sin of this lane's elements as bf16 pairs (.to(q.dtype), rope.py:106-107)
+  uint32_t c2[kWords], s2[kWords];
 #pragma unroll
   for (int e = 0; e < VEC; e += 4) {
     const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d + e);
     const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d + e);
-    cf[e] = c4.x; cf[e + 1] = c4.y; cf[e + 2] = c4.z; cf[e + 3] = c4.w;
-    sf[e] = s4.x; sf[e + 1] = s4.y; sf[e + 2] = s4.z; sf[e + 3] = s4.w;
+    c2[e / 2] = b200::pack_bf16x2(c4.x, c4.y);
+    c2[e / 2 + 1] = b200::pack_bf16x2(c4.z, c4.w);
+    s2[e / 2] = b200::pack_bf16x2(s4.x, s4.y);
+    s2[e / 2 + 1] = b200::pack_bf16x2(s4.z, s4.w);
   }
-#pragma unroll
-  for (int e = 0; e < VEC; e += 2) {
-    bf16_round2(cf[e], cf[e + 1]);
-    bf16_round2(sf[e], sf[e + 1]);
-  }
+  // rotate_half negates the partner for the first half of the row
+  const uint32_t neg = li < kLanesPerRow / 2 ? 0x80008000u : 0u;
 
   int64_t k_off = 0, v_off = 0;
   const bool kv_rows = h0 + nrows > a.num_heads;
@@ -177,48 +191,34 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const P
     const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw[i]);
     // the reduction and the RoPE exchange are shuffles over the whole warp,
     // so every lane takes part; v rows and dead rows contribute zeros
-    float x[VEC];
-#pragma unroll
-    for (int w = 0; w < kWords; ++w) {
-      x[2 * w] = b200::bf16_lo(rw[w]);
-      x[2 * w + 1] = b200::bf16_hi(rw[w]);
-    }
     const bool norm = live && (is_q || is_k);
     // RMSNorm in fp32: mean of squares over the 128 elements of the row
     float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) ss = fmaf(x[e], x[e], ss);
+    for (int w = 0; w < kWords; ++w) {
+      const float x0 = b200::bf16_lo(rw[w]), x1 = b200::bf16_hi(rw[w]);
+      ss = fmaf(x0, x0, ss);
+      ss = fmaf(x1, x1, ss);
+    }
     if (!norm) ss = 0.f;
 #pragma unroll
     for (int o = kLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float rms = __frsqrt_rn(ss / static_cast<float>(kD) + a.eps);
+    const uint64_t rms2 = b200::f2_pack(rms, rms);
     const __nv_bfloat16* wp = (is_q ? a.q_w : a.k_w) + d;
-    Vec wv = *reinterpret_cast<const Vec*>(wp);
+    const Vec wv = *reinterpret_cast<const Vec*>(wp);
     const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
-    float y[VEC];
+    // y = bf16((x * rms) * w), then RoPE: bf16(bf16(y * c) + bf16(rot(y) * s))
+    uint32_t out_w[kWords];
 #pragma unroll
     for (int w = 0; w < kWords; ++w) {
-      y[2 * w] = (x[2 * w] * rms) * b200::bf16_lo(ww[w]);
-      y[2 * w + 1] = (x[2 * w + 1] * rms) * b200::bf16_hi(ww[w]);
-      bf16_round2(y[2 * w], y[2 * w + 1]);
+      float y0, y1;
+      b200::f2_unpack(b200::f2_mul(b200::f2_mul(bf2_to_f2(rw[w]), rms2), bf2_to_f2(ww[w])), y0, y1);
+      const uint32_t y2 = b200::pack_bf16x2(y0, y1);
+      const uint32_t rot = __shfl_xor_sync(0xffffffffu, y2, kLanesPerRow / 2) ^ neg;
+      out_w[w] = bf2_add(bf2_mul(y2, c2[w]), bf2_mul(rot, s2[w]));
     }
-    // RoPE: partner elements d +- 64 live in lane ^ (lanes per row / 2)
-    float yc[VEC], rs[VEC];
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float p = __shfl_xor_sync(0xffffffffu, y[e], kLanesPerRow / 2);
-      const float rot = li < kLanesPerRow / 2 ? -p : p;
-      yc[e] = y[e] * cf[e];
-      rs[e] = rot * sf[e];
-    }
-    uint32_t packed[kWords];
-#pragma unroll
-    for (int w = 0; w < kWords; ++w) {
-      bf16_round2(yc[2 * w], yc[2 * w + 1]);
-      bf16_round2(rs[2 * w], rs[2 * w + 1]);
-      packed[w] = b200::pack_bf16x2(yc[2 * w] + rs[2 * w], yc[2 * w + 1] + rs[2 * w + 1]);
-    }
-    const Vec out = *reinterpret_cast<const Vec*>(packed);
+    const Vec out = *reinterpret_cast<const Vec*>(out_w);
     if (!live) continue;
     if (is_q) {
       *reinterpret_cast<Vec*>(a.q_out + b * a.qo_b + hh * a.qo_h + s * a.qo_s + d) = out;
@@ -293,8 +293,8 @@ extern "C" int b200_qk_norm_rope_kv_write(
   const int heads = num_heads + (pool ? 2 : 1) * num_kv_heads;
   const int64_t warps =
       static_cast<int64_t>(batch) * n_tokens * ((heads + kRowsPerWarp - 1) / kRowsPerWarp);
+  if (warps > 0x7fffffff - kWarps) return B200_ERR_INVALID_ARGUMENT;
   const int64_t blocks = (warps + kWarps - 1) / kWarps;
-  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
 
   PrologueArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -347,6 +347,7 @@ extern "C" int b200_qk_norm_rope_kv_write(
   a.max_pages = max_pages;
   a.max_requests = max_requests;
   a.layer = layer;
+  a.total_warps = static_cast<int>(warps);
   a.dev_status = dev_status;
   // 16-byte row pieces when every row and the weights allow them
   bool v16 = b200host::aligned16(q) && b200host::aligned16(k) && b200host::aligned16(q_weight) &&

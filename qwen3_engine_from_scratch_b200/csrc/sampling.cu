@@ -14,9 +14,14 @@
 //       (top_k == 0, top_p >= 1: logit / T + Gumbel noise at offset row * V + j;
 //       the reference draws these with torch.multinomial, :81-109, another
 //       stream); k_sel = 1 for greedy and temperature-only rows, else top_k.
+//       For k_sel <= 64 the bit-by-bit search is replaced by a lower bound
+//       (the k-th largest of the threads' maxima), a compaction of the few
+//       entries at or above it, and a direct ranking of those.
 //   row kernel    grid (rows): the same selection over the chunks'
 //       candidates, a bitonic sort by (score desc, index asc), and for top-k
-//       rows the reference kernel's arithmetic on the sorted candidates:
+//       rows the reference kernel's arithmetic on the sorted candidates
+//       (sample_row_fast_kernel when every k of the batch is at most 64:
+//       bound, compaction and ranking again, then one warp's scans):
 //       x = logit / T, softmax, keep[0] | cumsum(p)[j-1] <= top_p, Gumbel-max
 //       with the uniform of Triton's tl.rand(seed, row * block_k + j)
 //       (Philox4x32-10, key = seed, counter = (offset, 0, 0, 0), first word to
@@ -342,6 +347,33 @@ B200_DEVICE uint64_t block_top1(const uint32_t (&key)[PER], uint64_t* red64) {
 
 constexpr int kChunkThreads = 512;
 constexpr int kChunkPer = kChunk / kChunkThreads;  // 16 logits per thread
+// Rows selecting at most kFastK per chunk first bound the k-th largest key
+// from below by the k-th largest of the threads' maxima (k distinct entries
+// reach it), keep only the entries at or above that bound (the k best are
+// among them; for k <= kFastK at most kFastK * kChunkPer = kMaxK unless the
+// bound is tied) and rank those few directly: a handful of barriers instead
+// of one per key bit.
+constexpr int kFastK = kMaxK / kChunkPer;          // 64
+
+// k-th largest of the block's per-thread values v (top bits only: values
+// >> low), by one warp's bit-by-bit search over the kChunkThreads values in
+// shared memory; warp reductions only.
+B200_DEVICE uint32_t warp_kth_of(const uint32_t* v, int k, int low) {
+  constexpr int kPerLane = kChunkThreads / 32;
+  const int lane = threadIdx.x & 31;
+  uint32_t x[kPerLane];
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) x[i] = v[lane * kPerLane + i];
+  uint32_t t = 0;
+  for (int b = 31 - low; b >= 0; --b) {
+    const uint32_t cand = t | (1u << b);
+    int c = 0;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) c += x[i] >= cand ? 1 : 0;
+    if (__reduce_add_sync(0xffffffffu, c) >= k) t = cand;
+  }
+  return t;
+}
 
 // One chunk of one row: its k_sel best scores into the workspace.
 __global__ void __launch_bounds__(kChunkThreads) sample_chunk_kernel(const SampleArgs a) {
@@ -417,6 +449,60 @@ __global__ void __launch_bounds__(kChunkThreads) sample_chunk_kernel(const Sampl
   const int k = min(k_sel, n);
   // bf16 scores leave the low 16 key bits constant (greedy / top-k rows)
   const int low = (a.bf16 && mode != kTempOnly) ? 16 : 0;
+  if (k <= kFastK) {
+    __shared__ uint32_t tmax[kChunkThreads];
+    __shared__ uint32_t s_bound;
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < kChunkPer; ++i) m = max(m, key[i] >> low);
+    tmax[tid] = m;
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    if (tid < 32) {
+      const uint32_t t0 = warp_kth_of(tmax, k, low);
+      if (tid == 0) s_bound = t0;
+    }
+    __syncthreads();
+    const uint32_t bound = s_bound;
+    // entries at or above the bound (real keys only) into c[], one atomic per warp
+    int cnt = 0;
+#pragma unroll
+    for (int i = 0; i < kChunkPer; ++i) cnt += (key[i] != 0u && (key[i] >> low) >= bound) ? 1 : 0;
+    const int lane = tid & 31;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int base = 0;
+    if (lane == 31) base = atomicAdd(&s_count, incl);
+    int pos = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
+#pragma unroll
+    for (int i = 0; i < kChunkPer; ++i) {
+      if (key[i] != 0u && (key[i] >> low) >= bound) {
+        if (pos < kMaxK)
+          c[pos] = (static_cast<uint64_t>(key[i]) << 32) |
+                   static_cast<uint32_t>(~ident(tid * kChunkPer + i));
+        ++pos;
+      }
+    }
+    __syncthreads();
+    const int cn = s_count;
+    if (cn <= kMaxK) {
+      // rank of each entry among all of them, by (key desc, index asc): the
+      // k best land sorted in dst[0..k)
+      for (int i = tid; i < cn; i += kChunkThreads) {
+        const uint64_t v = c[i];
+        int r = 0;
+        for (int j2 = 0; j2 < cn; ++j2) r += c[j2] > v ? 1 : 0;
+        if (r < k) dst[r] = v;
+      }
+      for (int i = k + tid; i < k_sel; i += kChunkThreads) dst[i] = 0;
+      return;
+    }
+    // a bound tied across many threads: the general search below
+  }
   select_k<kChunkThreads, kChunkPer>(key, k, low, ident, c, red, &s_count);
   // sorted by (score desc, index asc): the row kernel then meets equal scores
   // in ascending vocabulary order (chunks in order, each chunk sorted)
@@ -500,6 +586,140 @@ __global__ void __launch_bounds__(kThreads) sample_row_kernel(const SampleArgs a
   (void)mode;
 }
 
+// One row per CTA, for batches whose every k is at most kFastK: the same
+// selection and arithmetic as sample_row_kernel with a handful of barriers.
+// The chunks' lists are sorted, so the k-th largest of their first
+// ceil(k / chunks) entries bounds the row's k-th largest candidate from below
+// (k sampled entries reach it); the candidates at or above the bound are
+// ranked directly in the total order (key desc, index asc), which puts the k
+// best sorted in place; one warp then takes the reference kernel's step.
+constexpr int kRowFastThreads = 256;
+constexpr int kRowFastMax = kMaxChunks * kFastK;  // every candidate of a row
+
+__global__ void __launch_bounds__(kRowFastThreads) sample_row_fast_kernel(const SampleArgs a) {
+  __shared__ __align__(16) uint64_t sel[kRowFastMax];
+  __shared__ __align__(16) uint64_t samp[kFastK + kMaxChunks];
+  __shared__ __align__(16) uint64_t cand[kFastK];
+  __shared__ uint64_t s_bound;
+  __shared__ int s_count;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  int k;
+  row_mode(a, row, &k, false);
+  k = min(k, a.block_k);
+  const uint64_t* src = a.cand + static_cast<int64_t>(row) * a.chunks * a.block_k;
+  const int n = a.chunks * k;
+  auto ent = [&](int c) { return src[(c / k) * a.block_k + (c % k)]; };
+  if (k == 1) {
+    if (tid < 32) {
+      uint64_t best = 0;
+      for (int c = lane; c < n; c += 32) {
+        const uint64_t v = ent(c);
+        best = v > best ? v : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t y = __shfl_xor_sync(0xffffffffu, best, o);
+        best = y > best ? y : best;
+      }
+      if (lane == 0) a.out[row] = static_cast<int>(~static_cast<uint32_t>(best));
+    }
+    return;
+  }
+  // the bound: the k-th largest of the first r entries of every chunk
+  const int r = (k + a.chunks - 1) / a.chunks;
+  const int ns = a.chunks * r;
+  if (tid < ns) samp[tid] = src[(tid / r) * a.block_k + (tid % r)];
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+  if (tid < ns) {
+    const uint64_t v = samp[tid];
+    int rk = 0;
+    for (int j = 0; j < ns; ++j) rk += samp[j] > v ? 1 : 0;
+    if (rk == k - 1) s_bound = v;
+  }
+  __syncthreads();
+  const uint64_t bound = s_bound;
+  // every candidate at or above the bound, one shared atomic per warp and pass
+  for (int c0 = 0; c0 < n; c0 += kRowFastThreads) {
+    const int c = c0 + tid;
+    const uint64_t v = c < n ? ent(c) : 0;
+    const bool take = c < n && v >= bound;
+    const uint32_t bal = __ballot_sync(0xffffffffu, take);
+    int base = 0;
+    if (lane == 0 && bal != 0u) base = atomicAdd(&s_count, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (take) sel[base + __popc(bal & ((1u << lane) - 1u))] = v;
+  }
+  __syncthreads();
+  const int cn = s_count;
+  for (int i = tid; i < cn; i += kRowFastThreads) {
+    const uint64_t v = sel[i];
+    int rk = 0;
+    for (int j = 0; j < cn; ++j) rk += sel[j] > v ? 1 : 0;
+    if (rk < k) cand[rk] = v;
+  }
+  __syncthreads();
+  if (tid >= 32) return;
+
+  // ---- the reference kernel's step on the sorted candidates (ranks lane, lane + 32)
+  const void* lg = a.bf16 ? static_cast<const void*>(static_cast<const __nv_bfloat16*>(a.logits) +
+                                                     row * a.stride)
+                          : static_cast<const void*>(static_cast<const float*>(a.logits) +
+                                                     row * a.stride);
+  const float temp = row_temperature(a, row);
+  const float top_p = row_top_p(a, row);
+  float x[2], e[2];
+  int idx[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int j = lane + 32 * h;
+    idx[h] = j < k ? static_cast<int>(~static_cast<uint32_t>(cand[j])) : 0;
+    x[h] = j < k ? logit_at(a, lg, idx[h]) / temp : -INFINITY;
+  }
+  const float m0 = __shfl_sync(0xffffffffu, x[0], 0);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) e[h] = lane + 32 * h < k ? expf(x[h] - m0) : 0.f;
+  // inclusive scan over the ranks (lane order, then the second half)
+  auto scan2 = [&](const float (&v)[2], float (&out)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float sum = v[h];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, sum, o);
+        if (lane >= o) sum += y;
+      }
+      out[h] = sum;
+    }
+    out[1] += __shfl_sync(0xffffffffu, out[0], 31);
+  };
+  float ce[2];
+  scan2(e, ce);
+  const float total = __shfl_sync(0xffffffffu, ce[1], 31);
+  float p[2], cp[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) p[h] = e[h] / total;
+  scan2(p, cp);
+  ArgMax best{-INFINITY, 0x7fffffff};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int j = lane + 32 * h;
+    const bool keep = j < k && (j == 0 || cp[h] - p[h] <= top_p);
+    const float score =
+        keep ? x[h] + gumbel(a.seed, static_cast<uint64_t>(row) * a.block_k + j) : -INFINITY;
+    best = better(best, ArgMax{score, j});
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax y;
+    y.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+    y.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+    best = better(best, y);
+  }
+  const int bidx = __shfl_sync(0xffffffffu, best.i < 32 ? idx[0] : idx[1], best.i & 31);
+  if (lane == 0) a.out[row] = bidx;
+}
+
 int chunks_for(int vocab) { return (vocab + kChunk - 1) / kChunk; }
 
 }  // namespace
@@ -548,7 +768,9 @@ extern "C" int b200_sample_tokens(const void* logits, int logits_bf16, int64_t s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   sample_chunk_kernel<<<dim3(chunks, batch), kChunkThreads, 0, s>>>(a);
   const int cand_per_row = chunks * block_k;
-  if (cand_per_row <= kThreads) {
+  if (block_k <= kFastK) {
+    sample_row_fast_kernel<<<batch, kRowFastThreads, 0, s>>>(a);
+  } else if (cand_per_row <= kThreads) {
     sample_row_kernel<1><<<batch, kThreads, 0, s>>>(a);
   } else if (cand_per_row <= 2 * kThreads) {
     sample_row_kernel<2><<<batch, kThreads, 0, s>>>(a);

@@ -73,6 +73,37 @@ def test_ties_at_the_topk_threshold(cuda, native_lib):
     assert np.array_equal(out[:, 0].cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_small_k_batch_vs_oracle(dtype, cuda, native_lib):
+    """Every k <= 64: the chunks take the bound-and-rank selection and the rows
+    the one-warp kernel; tokens equal the oracle's (Qwen3 vocabulary)."""
+    import qwen3_engine_from_scratch_b200 as qb
+    g = torch.Generator(device=cuda).manual_seed(16)
+    B, V = 64, 151936
+    logits = (torch.randn(B, V, generator=g, device=cuda) * 3).to(dtype)
+    temps = [0.7, 1.0, 1.5, 0.3, 0.0, 1.2, 0.9, 0.5] * 8
+    ks = [50, 1, 20, 64, 7, 33, 2, 16] * 8
+    ps = [0.9, 1.0, 0.8, 0.95, 0.5, 1.0, 0.99, 0.7] * 8
+    out = qb.sample_tokens(logits, temps, ks, ps, seed=99)
+    torch.cuda.synchronize()
+    want = osmp.sample_tokens(logits.float().cpu().numpy(), temps, ks, ps, 99)
+    assert np.array_equal(out[:, 0].cpu().numpy(), want)
+
+
+def test_small_k_ties_vs_oracle(cuda, native_lib):
+    """Coarsely quantised logits with k <= 64: the threads' maxima tie at the
+    bound, so some chunks fall back to the bit-by-bit search; the lowest
+    indices are kept at the threshold."""
+    import qwen3_engine_from_scratch_b200 as qb
+    g = torch.Generator(device=cuda).manual_seed(17)
+    logits = torch.round(torch.randn(16, 40000, generator=g, device=cuda) * 2) / 2
+    ks = [10, 33, 64, 5] * 4
+    out = qb.sample_tokens(logits, 1.0, ks, 1.0, seed=78)
+    torch.cuda.synchronize()
+    want = osmp.sample_tokens(logits.cpu().numpy(), 1.0, ks, 1.0, 78)
+    assert np.array_equal(out[:, 0].cpu().numpy(), want)
+
+
 def _tv(counts, probs):
     return 0.5 * np.abs(counts / counts.sum() - probs).sum()
 
