@@ -31,7 +31,9 @@
 // Every CTA builds the same work list in shared memory: only the non-empty
 // items, sequence-major (longest sequence first), heaviest tile first within
 // a sequence; items are taken from a global counter (dynamic balance) or,
-// without one, in a fixed boustrophedon order.  KV tiles strictly above the
+// without one, in a fixed boustrophedon order.  The scheduler lane decodes
+// each item once and passes its fields to the other roles through a 4-slot
+// ring in shared memory.  KV tiles strictly above the
 // diagonal are never loaded (the reference computes every KV block of the
 // sequence, flash_attention_varlen.py:74-77).
 //
@@ -438,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ Barriers B;
   __shared__ WorkList W;
+  __shared__ Item ring_item[kRing];  // the decoded items of the ring's slots
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -505,10 +508,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
 
-  // the roles read the n-th item of this CTA from the ring (-1 ends the list)
-  auto next_item = [&](int n, bool& ok) -> int {
+  // the roles read the n-th item of this CTA from the ring, index and fields
+  // as the scheduler decoded them (-1 ends the list)
+  auto next_item = [&](int n, bool& ok, Item& it) -> int {
     ok = wait_or_flag(bar_rf(n), (n / kRing) & 1, &B, a.dev_status);
     const int k = ok ? W.ring[n & (kRing - 1)] : -1;
+    if (k >= 0) it = ring_item[n & (kRing - 1)];
     mbar_arrive(bar_re(n));
     return k;
   };
@@ -532,10 +537,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (k >= W.n_items) k = -1;
         if (n >= kRing && !(ok = wait_or_flag(bar_re(n), ((n / kRing) - 1) & 1, &B, a.dev_status)))
           break;
+        Item it;
+        if (k >= 0) {
+          it = decode_item(a, W, k);
+          ring_item[n & (kRing - 1)] = it;
+        }
         W.ring[n & (kRing - 1)] = k;
         mbar_arrive(bar_rf(n));
         if (k < 0) break;
-        const Item it = decode_item(a, W, k);
         if (n > 0 && !(ok = wait_or_flag(bar_qe, (n - 1) & 1, &B, a.dev_status))) break;
         b200::mbar_arrive_expect_tx(bar_q, 2 * kQBytes);
 #pragma unroll
@@ -569,9 +578,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int gs = 0;  // steps of this CTA before the current item
       bool ok = true;
       for (int n = 0; ok; ++n) {
-        const int k = next_item(n, ok);
+        Item it;
+        const int k = next_item(n, ok, it);
         if (!ok || k < 0) break;
-        const Item it = decode_item(a, W, k);
         const int g_last = gs + it.n_kv - 1;
         gs += it.n_kv;
         // The lead of the softmax over this lane is bounded: the stage this
@@ -581,9 +590,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < 2 && ok; ++t) {
           if (!(ok = wait_or_flag(bar_st(t, n), (n >> 1) & 1, &B, a.dev_status))) break;
           const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
-          if (it.m0[t] + kBM <= it.len) {
-            b200::tma_store_3d(&tmo, stage, 0, it.h[t], it.start + it.m0[t]);
-            b200::tma_store_3d(&tmo, stage + kKVBlock, 64, it.h[t], it.start + it.m0[t]);
+          const int m0t = t == 0 ? it.m0[0] : it.m0[1];
+          const int ht = t == 0 ? it.h[0] : it.h[1];
+          if (m0t + kBM <= it.len) {
+            b200::tma_store_3d(&tmo, stage, 0, ht, it.start + m0t);
+            b200::tma_store_3d(&tmo, stage + kKVBlock, 64, ht, it.start + m0t);
             b200::bulk_commit_group();
             b200::bulk_wait_group_read0();
           }
@@ -597,9 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int vc = 0;
       bool ok = true;
       for (int n = 0; ok; ++n) {
-        const int k = next_item(n, ok);
+        Item it;
+        const int k = next_item(n, ok, it);
         if (!ok || k < 0) break;
-        const Item it = decode_item(a, W, k);
         for (int j = 0; j < it.n_kv; ++j, ++vc) {
           const int s = vc & 1;
           if (vc >= kStages &&
@@ -645,9 +656,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;  // K/V tiles consumed by this CTA before the current item
       bool ok = true;
       for (int n = 0; ok; ++n) {
-        const int k = next_item(n, ok);
+        Item it;
+        const int k = next_item(n, ok, it);
         if (!ok || k < 0) break;
-        const Item it = decode_item(a, W, k);
         if (!(ok = wait_or_flag(bar_q, n & 1, &B, a.dev_status))) break;
         tc_fence_after();
         // step j issues P_t(j-1).V(j-1) then S_t(j) for t = 0, 1: S_t(j)
@@ -717,11 +728,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g = 0;
     bool ok = true;
     for (int n = 0; ok; ++n) {
-      const int k = next_item(n, ok);
+      Item it;
+      const int k = next_item(n, ok, it);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || k < 0) break;
-      const Item it = decode_item(a, W, k);
-      const int qpos = it.m0[t] + r;  // position within the sequence
+      // this tile's fields by selection, not by a runtime index (which would
+      // put the item in local memory)
+      const int m0t = t == 0 ? it.m0[0] : it.m0[1];
+      const int ht = t == 0 ? it.h[0] : it.h[1];
+      const int qpos = m0t + r;  // position within the sequence
       float m_used = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j, ++g) {
         ok = __all_sync(0xffffffffu, wait_or_flag(bar_sf(t), g & 1, &B, a.dev_status));
@@ -839,7 +854,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t stage = (t == 0 ? sK : sV) + (g_last & 1) * kKVBytes;
       // (paged mode: every tile row by row; its K/V stages, filled from 16
       // page boxes each, go back to their producers without waiting for this)
-      if (!a.paged && it.m0[t] + kBM <= it.len) {
+      if (!a.paged && m0t + kBM <= it.len) {
         // a full tile: rows staged in the swizzled [128 rows][64 d] x 2 layout
         // of a K/V tile (the TMA engine writes whole lines; the memory-
         // instruction queue that the other tile's softmax and the MMA thread
@@ -868,7 +883,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (qpos < it.len) {
         const float inv = 1.f / l;
         __nv_bfloat16* orow = a.out + static_cast<int64_t>(it.start + qpos) * a.o_t +
-                              static_cast<int64_t>(it.h[t]) * a.o_h;
+                              static_cast<int64_t>(ht) * a.o_h;
         if (a.out32) {
           // 32-byte stores: every row piece is a full sector
 #pragma unroll
