@@ -44,7 +44,8 @@
 //   P     A operand in TMEM: lane = query row, column c = keys 2c, 2c+1.
 //   V (128 keys x 128 d)  MN-major (d contiguous), 128B swizzle: LBO = 16 KB
 //         between the two 64-d blocks, SBO = 1024 B (8 keys), start += 2 KB
-//         (16 keys) per K step.
+//         (16 keys) per K step.  Paged mode: one 4 KB block per page
+//         ([d half][16 keys][64 d]), LBO = 2 KB, start += 4 KB per K step.
 //   TMEM  columns [0,128) S0/P0, [128,256) S1/P1, [256,384) O0, [384,512) O1;
 //         lane = query row.
 // MMAs issued by the one MMA thread execute in order, so S_t(j+1) overwriting
@@ -249,6 +250,17 @@ B200_DEVICE void umma_commit(uint32_t bar) {
       : "memory");
 }
 
+// 5-D tiled tensor load (no multicast), completing on `bar`.
+B200_DEVICE void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                             int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(c4)
+      : "memory");
+}
+
 B200_DEVICE void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -324,13 +336,18 @@ B200_DEVICE bool wait_or_flag(uint32_t bar, uint32_t parity, Barriers* B, int32_
   return false;
 }
 
-// Paged mode: key tile j (keys [128j, 128j + 128)) of an item from the pool,
-// 8 pages x two 64-column boxes of [16 slots][64 d] (2 KB each, stacked in the
-// canonical [128 keys][64 d] block).  Pages past the sequence repeat its last
-// page, so masked keys read finite data; a bad table entry is flagged and
-// replaced by block 0.
+// Paged mode: key tile j (keys [128j, 128j + 128)) of an item from the pool.
+// K: 8 pages x two 64-column boxes of [16 slots][64 d] (2 KB each, stacked in
+// the canonical [128 keys][64 d] blocks: the S MMA's B operand needs its
+// 8-key groups at one stride across all 128 keys).  V (v_pages): one 4 KB box
+// per page, [d half][16 slots][64 d], through a 5-D map whose d-half
+// dimension (stride 128 B) comes after the slot dimension; each P.V MMA
+// reads 16 keys, one page, so its descriptor starts at the page and steps
+// 2 KB between the d halves.  Pages past the sequence repeat its last page,
+// so masked keys read finite data; a bad table entry is flagged and replaced
+// by block 0.
 B200_DEVICE void load_kv_tile_paged(const PrefillArgs& a, const Item& it, const CUtensorMap* map,
-                                    uint32_t dst, uint32_t bar, int j) {
+                                    uint32_t dst, uint32_t bar, int j, bool v_pages = false) {
   const int last_page = (it.ctx + it.len - 1) / 16;
   const int32_t* bt = a.block_table + static_cast<int64_t>(it.row) * a.bt_row;
   int phys[kBN / 16];
@@ -343,6 +360,11 @@ B200_DEVICE void load_kv_tile_paged(const PrefillArgs& a, const Item& it, const 
       ph = 0;
     }
     phys[i] = ph;
+  }
+  if (v_pages) {
+#pragma unroll
+    for (int i = 0; i < kBN / 16; ++i) tma_load_5d(dst + i * 4096, map, bar, 0, 0, 0, it.hk, phys[i]);
+    return;
   }
 #pragma unroll
   for (int i = 0; i < kBN / 16; ++i) {
@@ -619,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t dv = sV + s * kKVBytes;
           b200::mbar_arrive_expect_tx(bar_v(s), kKVBytes);
           if (a.paged) {
-            load_kv_tile_paged(a, it, &tmv, dv, bar_v(s), j);
+            load_kv_tile_paged(a, it, &tmv, dv, bar_v(s), j, true);
           } else {
             b200::tma_load_3d(dv, &tmv, bar_v(s), 0, it.hk, it.start + j * kBN);
             b200::tma_load_3d(dv + kKVBlock, &tmv, bar_v(s), 64, it.hk, it.start + j * kBN);
@@ -647,9 +669,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int t, int s, bool accumulate) {
         const uint32_t vt = sV + s * kKVBytes;
 #pragma unroll
+        // packed V: [d half][128 keys][64 d] (halves 16 KB apart); paged V:
+        // [page][d half][16 keys][64 d] (4 KB per page, halves 2 KB apart)
+        const uint32_t kstep = a.paged ? 4096u : 16u * 128u;
+        const uint32_t lbo = a.paged ? 2048u : static_cast<uint32_t>(kKVBlock);
+#pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           umma_bf16_ts(tmem + kColO + t * kD, tmem + kColS + t * kBN + kk * 8,
-                       smem_desc(vt + kk * 16 * 128, kKVBlock, 1024), idO,
+                       smem_desc(vt + kk * kstep, lbo, 1024), idO,
                        (accumulate || kk > 0) ? 1u : 0u);
         }
       };
@@ -1115,7 +1142,8 @@ extern "C" int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_s
   int st = encode_rows_map(&tq, q, num_heads, total_tokens, q_stride_t, q_stride_h, kBM);
   if (st != B200_OK) return st;
   {
-    // one layer of the pool: (d = 128, slot = 16, kv head, block), boxes of one page
+    // K, one layer of the pool: (d = 128, slot = 16, kv head, block), boxes of
+    // half a page
     const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), 16u,
                                 static_cast<cuuint64_t>(num_kv_heads),
                                 static_cast<cuuint64_t>(num_blocks)};
@@ -1127,9 +1155,19 @@ extern "C" int b200_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_s
     if (b200host::encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                                const_cast<void*>(k_pool), dims, strides_b, box, es,
                                CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS ||
-        b200host::encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
-                               const_cast<void*>(v_pool), dims, strides_b, box, es,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS)
+      return B200_ERR_TENSOR_MAP;
+    // V: one box per page, (d 64, slot 16, d half 2, kv head, block) -> smem
+    // [d half][slot][64 d]
+    const cuuint64_t dims5[5] = {64u, 16u, 2u, static_cast<cuuint64_t>(num_kv_heads),
+                                 static_cast<cuuint64_t>(num_blocks)};
+    const cuuint64_t strides5[4] = {static_cast<cuuint64_t>(kv_stride_slot) * 2, 128u,
+                                    static_cast<cuuint64_t>(kv_stride_h) * 2,
+                                    static_cast<cuuint64_t>(kv_stride_blk) * 2};
+    const cuuint32_t box5[5] = {64, 16, 2, 1, 1};
+    const cuuint32_t es5[5] = {1, 1, 1, 1, 1};
+    if (b200host::encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5,
+                               const_cast<void*>(v_pool), dims5, strides5, box5, es5,
                                CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B) != CUDA_SUCCESS)
       return B200_ERR_TENSOR_MAP;
