@@ -936,6 +936,7 @@ def bench_prologue(torch, ops, device, g, T, H, Hkv, D, steps, warmup, peaks):
     gbs = nbytes / (f_ms / 1e3) / 1e9
     return {"kernel": "qk_norm_rope_kv_write_kernel", "tokens": T, "ms": round(f_ms, 4),
             "bytes": nbytes, "gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "traffic": read_traffic("qk_norm_rope_kv_write_kernel"),
             "unfused_ms": round(u_ms, 4), "speedup_vs_unfused": round(u_ms / f_ms, 2),
             "unfused": "the reference's RMSNorm x2 + apply_rotary_pos_emb in torch ops, then "
                        "kv_scatter_rows"}
@@ -1183,7 +1184,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "sampling"],
+                    help="sampling: only the fused sampler's leg (a small case for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-prefill", action="store_true")
@@ -1212,7 +1214,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.config == "c3":
+        if args.config == "sampling":
+            torch.cuda.set_device(local_rank)
+            line = bench_sampling(torch.device("cuda", local_rank)) if rank == 0 else None
+        elif args.config == "c3":
             torch.cuda.set_device(local_rank)
             r = run_prefill(args, rank, world, local_rank, steps=args.steps, warmup=args.warmup,
                             headline=True)
