@@ -116,8 +116,11 @@ B200_DEVICE uint64_t bf2_to_f2(uint32_t w) {
 // the rsqrt, the weights) is spread over twice the elements.  After the
 // normalisation every value is a packed bf16 pair: the RoPE partner is
 // exchanged as pairs and the products and the sum are packed bf16 operations.
+// The launch bound of 4 CTAs per SM keeps the kernel at 64 registers without
+// spills: at 3 CTAs (67 registers) it was bound by the warps it could keep in
+// flight.
 template <int VEC>
-__global__ void __launch_bounds__(kThreads) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
   constexpr int kLanesPerRow = kD / VEC;        // 16 or 32
   constexpr int kRowsPerPass = 32 / kLanesPerRow;
   constexpr int kPasses = kRowsPerWarp / kRowsPerPass;
