@@ -375,8 +375,11 @@ B200_DEVICE uint32_t warp_kth_of(const uint32_t* v, int k, int low) {
   return t;
 }
 
-// One chunk of one row: its k_sel best scores into the workspace.
-__global__ void __launch_bounds__(kChunkThreads) sample_chunk_kernel(const SampleArgs a) {
+// One chunk of one row: its k_sel best scores into the workspace.  Three CTAs
+// per SM (40 registers; the few spills sit off the common path) keep more
+// chunks in flight than two at 64 registers: 35 -> 33 us for top-k 50,
+// 100 -> 94 us for top-k 200 on 64 x 151936 logits.
+__global__ void __launch_bounds__(kChunkThreads, 3) sample_chunk_kernel(const SampleArgs a) {
   __shared__ __align__(16) uint64_t c[kMaxK];
   __shared__ uint64_t red64[kChunkThreads / 32];
   __shared__ int red[2 * kChunkThreads / 32];
