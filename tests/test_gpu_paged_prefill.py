@@ -87,6 +87,22 @@ def test_context_and_chunk_boundaries_vs_oracle(H, Hkv, cuda, native_lib):
     _close(out, _oracle(c, scale))
 
 
+def test_bench_chunk_shape_vs_oracle(cuda, native_lib):
+    """The bench's chunk case: 32 sequences with U[0, 2048] cached tokens and a
+    new chunk of U[64, 512] each (16/8 heads), every sequence against the oracle."""
+    import qwen3_engine_from_scratch_b200 as qb
+    rng = np.random.default_rng(5000)
+    ctx = rng.integers(0, 2048, size=32, endpoint=True).tolist()
+    new = rng.integers(64, 512, size=32, endpoint=True).tolist()
+    c = _setup(cuda, ctx, new, 16, 8, seed=501)
+    scale = 1 / math.sqrt(D)
+    qb.clear_device_status()
+    out = _run(qb, c, scale)
+    torch.cuda.synchronize()
+    qb.check_device_status()
+    _close(out, _oracle(c, scale))
+
+
 def test_no_context_equals_varlen_prefill_bitexact(cuda, native_lib):
     """With nothing cached, the paged kernel reads the same K/V values the packed
     kernel reads, in the same tiles: outputs are bit-identical."""

@@ -111,8 +111,8 @@ def test_tile_boundaries_and_gqa(H, Hkv, cuda, native_lib):
 
 
 def test_config3_shape_vs_oracle(cuda, native_lib):
-    """Config 3: 32 sequences, L~U[64,2048], 16/8/128; oracle on 4 of them,
-    finiteness on all, and per-sequence independence (order permutation)."""
+    """Config 3: 32 sequences, L~U[64,2048], 16/8/128; every sequence against
+    the oracle, and per-sequence independence (order permutation)."""
     import qwen3_engine_from_scratch_b200 as qb
     rng = np.random.default_rng(3)
     lens = rng.integers(64, 2048, size=32, endpoint=True).tolist()
@@ -122,7 +122,7 @@ def test_config3_shape_vs_oracle(cuda, native_lib):
     out = qb.flash_attention_prefill(q, k, v, cu, scale, H, Hkv, D, max_seqlen=max(lens))
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
-    idx = [int(np.argmax(lens)), int(np.argmin(lens)), 0, 31]
+    idx = list(range(len(lens)))
     refs = _oracle_seqs(q, k, v, lens, idx, scale)
     cun = np.concatenate([[0], np.cumsum(lens)])
     for i, ref in zip(idx, refs):
