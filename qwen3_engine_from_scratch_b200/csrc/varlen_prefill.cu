@@ -3,7 +3,7 @@
 // (qwen3/kernels/flash_attention_varlen.py:25-123) and its host entry (:126-194).
 //
 // Persistent, one CTA per SM (192 KB of tiles in shared memory, all 512 TMEM
-// columns, 10 warps).  A work item is a PAIR of 128-row query tiles that read the same
+// columns, 12 warps).  A work item is a PAIR of 128-row query tiles that read the same
 // K/V rows: two query heads of one kv head at the same positions (GQA group
 // even), or two consecutive row tiles of one head (group odd).  Each 128-key
 // K/V tile is loaded once for both.  The two tiles ping-pong: while the
@@ -24,10 +24,17 @@
 //               per instruction, 8 instructions), O_t += P_t.V (M=128,
 //               N=128, 8 instructions) with P_t read from TMEM; each group
 //               ends with tcgen05.commit on an mbarrier.
-//   warp 9      TMA producer: lane 0 takes the work items and loads both Q
-//               tiles and the K tiles (2-stage ring), lane 1 the V tiles;
-//               lane 2 (store lane, not in paged mode) writes the staged
+//   warp 9      TMA producer (lane 0): takes the work items and loads both Q
+//               tiles and the K tiles (2-stage ring)
+//   warp 10     V tiles (lane 0)
+//   warp 11     store lane (lane 0, not in paged mode): writes the staged
 //               output tiles with TMA stores and returns their stages.
+//               The loads and stores sit in warps of their own so that one
+//               lane's waits never hold up another's (paged mode: 640 -> 702
+//               TFLOP/s); the softmax warpgroups (warps 0-7) raise their
+//               registers to 216 with setmaxnreg while warps 8-11 drop to 64
+//               (256 x 216 + 128 x 64 = 63,488 of the 384 x 168 the block is
+//               launched with), which keeps the softmax free of spills.
 // Every CTA builds the same work list in shared memory: only the non-empty
 // items, sequence-major (longest sequence first), heaviest tile first within
 // a sequence; items are taken from a global counter (dynamic balance) or,
@@ -75,10 +82,12 @@ constexpr int kOffK = kOffQ + 2 * kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kSmemTiles = kOffV + kStages * kKVBytes;  // 192 KB
 constexpr int kSmemBytes = kSmemTiles + 1024;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr int kSoftmaxThreads = 256;
 constexpr int kMmaWarp = 8;
-constexpr int kProducerWarp = 9;
+constexpr int kProducerWarp = 9;   // Q/K loads and the scheduler
+constexpr int kVWarp = 10;          // V loads
+constexpr int kStoreWarp = 11;      // output TMA stores
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 2 * kBN;  // + tile * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -530,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
 
+
   // the roles read the n-th item of this CTA from the ring, index and fields
   // as the scheduler decoded them (-1 ends the list)
   auto next_item = [&](int n, bool& ok, Item& it) -> int {
@@ -540,8 +550,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     return k;
   };
 
+  // registers: the softmax warpgroups (warps 0-7) take 216, the MMA / load /
+  // store warpgroup (warps 8-11) gives its share down to 64:
+  // 256 x 216 + 128 x 64 = 63,488 <= 384 x 168 at launch
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
   if (warp == kProducerWarp) {
-    // lane 0: scheduler, both Q tiles and the K tiles; lane 1: the V tiles.
+    // lane 0: scheduler, both Q tiles and the K tiles (the V tiles: warp 10).
     // A K (V) stage is refilled once both S (both P.V) that read it are done.
     if (lane == 0) {
       b200::prefetch_tensormap(&tmq);
@@ -590,7 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else if (lane == 2 && !a.paged) {
+    }
+  } else if (warp == kStoreWarp) {
+    if (lane == 0 && !a.paged) {
       // store lane (not in paged mode, whose epilogue writes rows directly
       // and whose stages the MMA thread releases): sends each finished tile's output (staged by its softmax
       // threads in the stage of the item's last K tile for tile 0, of its last
@@ -625,7 +642,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // the output stores are complete before the CTA ends
       b200::bulk_wait_group0();
-    } else if (lane == 1) {
+    }
+  } else if (warp == kVWarp) {
+    if (lane == 0) {
       b200::prefetch_tensormap(&tmv);
       int vc = 0;
       bool ok = true;
@@ -722,7 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         g += it.n_kv;
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;" ::: "memory");
     // ---------------------------------------------------------- softmax
     const int t = warp >> 2;            // tile of this warpgroup
     const int r = threadIdx.x & 127;    // query row in the tile == TMEM lane
@@ -873,7 +894,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Staging buffer of this tile: the stage of the item's last K tile for
       // tile 0 (o_done of tile 0 covers every S of the item, tile 1's last
       // included), the stage of its last V tile for tile 1 (o_done of tile 1
-      // covers both last P.V).  The store lane of the producer warp sends it
+      // covers both last P.V).  The store lane (warp 11) sends it
       // out with TMA stores and returns the stage to its producer; the stage's
       // next tile (the next item's second K / V tile) is needed only a step
       // later.
