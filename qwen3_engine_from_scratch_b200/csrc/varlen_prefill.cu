@@ -687,7 +687,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O_t (+)= P_t . V(s), P_t read from tile t's score buffer in TMEM
       auto issue_pv = [&](int t, int s, bool accumulate) {
         const uint32_t vt = sV + s * kKVBytes;
-#pragma unroll
         // packed V: [d half][128 keys][64 d] (halves 16 KB apart); paged V:
         // [page][d half][16 keys][64 d] (4 KB per page, halves 2 KB apart)
         const uint32_t kstep = a.paged ? 4096u : 16u * 128u;
