@@ -427,37 +427,70 @@ B200_DEVICE void build_work_list(const PrefillArgs& a, WorkList& W) {
     }
   }
   __syncthreads();
-  // bitonic sort, ascending key = descending tile count, then sequence id
-  for (int k = 2; k <= p2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < p2; i += kThreads) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint32_t x = W.key[i], y = W.key[ixj];
-          if ((x > y) == ((i & k) == 0)) {
-            W.key[i] = y;
-            W.key[ixj] = x;
-          }
+  // bitonic sort, ascending key = descending tile count, then sequence id;
+  // up to 32 sequences one warp sorts them in registers (no block barriers)
+  const int lane = threadIdx.x & 31;
+  if (p2 <= 32) {
+    if (threadIdx.x < 32) {
+      uint32_t v = lane < p2 ? W.key[lane] : 0xFFFFFFFFu;
+      for (int k = 2; k <= 32; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          const uint32_t o = __shfl_xor_sync(0xffffffffu, v, j);
+          const bool lower = (lane & j) == 0, asc = (lane & k) == 0;
+          v = (lower == asc) ? min(v, o) : max(v, o);
         }
       }
-      __syncthreads();
+      if (lane < p2) W.key[lane] = v;
+    }
+  } else {
+    for (int k = 2; k <= p2; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < p2; i += kThreads) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const uint32_t x = W.key[i], y = W.key[ixj];
+            if ((x > y) == ((i & k) == 0)) {
+              W.key[i] = y;
+              W.key[ixj] = x;
+            }
+          }
+        }
+        __syncthreads();
+      }
     }
   }
-  if (threadIdx.x == 0) {
+  // items before each sequence of the sorted order, and the padded adapter's
+  // zero rows before each sequence: prefix sums by one warp
+  if (threadIdx.x < 32) {
+    __syncwarp();
     const int per = items_per_step(a);
-    int acc = 0;
-    for (int r = 0; r < n; ++r) {
-      W.seq_prefix[r] = acc;
-      acc += seq_steps(a, W.qtiles[W.key[r] & 0xFFFFu]) * per;
+    int acc = 0, pad = 0;
+    for (int r0 = 0; r0 < n; r0 += 32) {
+      const int r = r0 + lane;
+      const int v = r < n ? seq_steps(a, W.qtiles[W.key[r] & 0xFFFFu]) * per : 0;
+      const int z = r < n && a.zero_pad && W.pad_ok[r] ? (a.max_seqlen - W.len[r]) * a.num_heads : 0;
+      int iv = v, iz = z;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int yv = __shfl_up_sync(0xffffffffu, iv, o);
+        const int yz = __shfl_up_sync(0xffffffffu, iz, o);
+        if (lane >= o) {
+          iv += yv;
+          iz += yz;
+        }
+      }
+      if (r < n) {
+        W.seq_prefix[r] = acc + iv - v;
+        W.pad_prefix[r] = pad + iz - z;
+      }
+      acc += __shfl_sync(0xffffffffu, iv, 31);
+      pad += __shfl_sync(0xffffffffu, iz, 31);
     }
-    W.seq_prefix[n] = acc;
-    W.n_items = acc;
-    int pad = 0;
-    for (int s2 = 0; s2 < n; ++s2) {
-      W.pad_prefix[s2] = pad;
-      pad += a.zero_pad && W.pad_ok[s2] ? (a.max_seqlen - W.len[s2]) * a.num_heads : 0;
+    if (lane == 0) {
+      W.seq_prefix[n] = acc;
+      W.n_items = acc;
+      W.pad_prefix[n] = pad;
     }
-    W.pad_prefix[n] = pad;
   }
   __syncthreads();
 }
@@ -567,8 +600,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // scheduler: the next item from the global counter, or without one
         // the fixed boustrophedon order over the CTAs
         const int round = n / static_cast<int>(gridDim.x);
+        // (with the counter, the first item of CTA b is item b and the counter
+        // hands out the items from gridDim.x on: no atomic before the first loads)
         int k = a.sched != nullptr
-                    ? atomicAdd(&a.sched[0], 1)
+                    ? (n == 0 ? static_cast<int>(blockIdx.x)
+                              : atomicAdd(&a.sched[0], 1) + static_cast<int>(gridDim.x))
                     : round * static_cast<int>(gridDim.x) +
                           ((round & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
         if (k >= W.n_items) k = -1;
