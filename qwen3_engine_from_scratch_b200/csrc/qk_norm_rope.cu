@@ -15,11 +15,13 @@
 // with rotate_half(y) = cat(-y[64:], y[:64]).  The cos/sin rows are the ones
 // the reference's RotaryEmbedding gathered (fp32, (B, S, D)).
 //
-// One warp per 8 (token, head) rows of one token.  With 16-byte aligned rows
-// a half-warp holds a row, lane l of it elements 8l..8l+7, and a pass covers
-// two rows; otherwise a warp holds a row, lane l elements 4l..4l+3.  The RoPE
-// partner of a lane is the lane half a row away (l ^ 8, or l ^ 16).  A warp
-// issues its 8 row loads and the token's cos/sin row before any math.  Rows of a
+// One warp per token: it converts the token's cos/sin row and finds its pool
+// slot once, then takes the token's rows 8 at a time (one warp per 8 rows cost
+// every warp that per-token work: 129.3 -> 108.9 us on the C3 tokens).  With
+// 16-byte aligned rows a half-warp holds a row, lane l of it elements
+// 8l..8l+7, and a pass covers two rows; otherwise a warp holds a row, lane l
+// elements 4l..4l+3.  The RoPE partner of a lane is the lane half a row away
+// (l ^ 8, or l ^ 16).  A warp issues a group's 8 row loads before its math.  Rows of a
 // token: the q heads, then the k heads, then (when a pool is given) the v
 // heads.  A k row goes to k_out (optional) and to the pool slot of its
 // position; a v row only to the pool.  Pool addressing is the rows mode of the KV write: position =
@@ -34,7 +36,7 @@ namespace {
 constexpr int kD = 128;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRowsPerWarp = 8;  // rows (q, k or v heads) of one token per warp
+constexpr int kRowsPerWarp = 8;  // rows (q, k or v heads) of one token per load group
 
 struct PrologueArgs {
   const __nv_bfloat16* q;
@@ -60,7 +62,7 @@ struct PrologueArgs {
   const int32_t* row_ids;
   int batch, n_tokens, num_heads, num_kv_heads, block_size, num_blocks, max_pages, max_requests,
       layer;
-  int total_warps;  // batch * n_tokens * row chunks (below 2^31)
+  int total_warps;  // batch * n_tokens: one warp per token (below 2^31)
   int32_t* dev_status;
 };
 
@@ -128,20 +130,35 @@ __global__ void __launch_bounds__(kThreads, 4) qk_norm_rope_kv_write_kernel(cons
   using Vec = typename std::conditional<VEC == 8, uint4, uint2>::type;
   const int lane = threadIdx.x & 31;
   const int heads = a.num_heads + (a.k_pool != nullptr ? 2 : 1) * a.num_kv_heads;
-  const int chunks = (heads + kRowsPerWarp - 1) / kRowsPerWarp;
-  // the host keeps the warp count below 2^31: 32-bit index arithmetic
-  const int gw = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-  if (gw >= a.total_warps) return;
-  const int tok = gw / chunks;
-  const int h0 = (gw - tok * chunks) * kRowsPerWarp;
+  // one warp per token: the token's cos/sin and pool slot once, then its rows
+  // 8 at a time; the host keeps the warp count below 2^31 (32-bit indices)
+  const int tok = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  if (tok >= a.total_warps) return;
   const int b = tok / a.n_tokens;
   const int s = tok - b * a.n_tokens;
   const int sub = lane / kLanesPerRow;          // row of the pass this lane works on
   const int li = lane % kLanesPerRow;
   const int d = VEC * li;
-  const int nrows = min(kRowsPerWarp, heads - h0);
+  // cos / sin of this lane's elements as bf16 pairs (.to(q.dtype), rope.py:106-107)
+  uint32_t c2[kWords], s2[kWords];
+#pragma unroll
+  for (int e = 0; e < VEC; e += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d + e);
+    const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d + e);
+    c2[e / 2] = b200::pack_bf16x2(c4.x, c4.y);
+    c2[e / 2 + 1] = b200::pack_bf16x2(c4.z, c4.w);
+    s2[e / 2] = b200::pack_bf16x2(s4.x, s4.y);
+    s2[e / 2 + 1] = b200::pack_bf16x2(s4.z, s4.w);
+  }
+  // rotate_half negates the partner for the first half of the row
+  const uint32_t neg = li < kLanesPerRow / 2 ? 0x80008000u : 0u;
 
-  // every row load of this warp is issued before any math (memory-level parallelism)
+  int64_t k_off = 0, v_off = 0;
+  bool write_pool = false, pool_done = false;
+
+  for (int h0 = 0; h0 < heads; h0 += kRowsPerWarp) {
+  const int nrows = min(kRowsPerWarp, heads - h0);
+  // every row load of this group is issued before any math (memory-level parallelism)
   Vec raw[kPasses];
 #pragma unroll
   for (int i = 0; i < kPasses; ++i) {
@@ -158,25 +175,11 @@ __global__ void __launch_bounds__(kThreads, 4) qk_norm_rope_kv_write_kernel(cons
       raw[i] = *reinterpret_cast<const Vec*>(src + d);
     }
   }
-  // cos / sin of this lane's elements as bf16 pairs (.to(q.dtype), rope.py:106-107)
-  uint32_t c2[kWords], s2[kWords];
-#pragma unroll
-  for (int e = 0; e < VEC; e += 4) {
-    const float4 c4 = *reinterpret_cast<const float4*>(a.cos + b * a.cs_b + s * a.cs_s + d + e);
-    const float4 s4 = *reinterpret_cast<const float4*>(a.sin + b * a.cs_b + s * a.cs_s + d + e);
-    c2[e / 2] = b200::pack_bf16x2(c4.x, c4.y);
-    c2[e / 2 + 1] = b200::pack_bf16x2(c4.z, c4.w);
-    s2[e / 2] = b200::pack_bf16x2(s4.x, s4.y);
-    s2[e / 2 + 1] = b200::pack_bf16x2(s4.z, s4.w);
+  if (!pool_done && h0 + nrows > a.num_heads) {
+    // the token's pool slot, once, after the first rows that need it were requested
+    write_pool = a.k_pool != nullptr && pool_slot(a, b, s, lane, &k_off, &v_off);
+    pool_done = true;
   }
-  // rotate_half negates the partner for the first half of the row
-  const uint32_t neg = li < kLanesPerRow / 2 ? 0x80008000u : 0u;
-
-  int64_t k_off = 0, v_off = 0;
-  const bool kv_rows = h0 + nrows > a.num_heads;
-  const bool write_pool =
-      kv_rows && a.k_pool != nullptr && pool_slot(a, b, s, lane, &k_off, &v_off);
-
 #pragma unroll
   for (int i = 0; i < kPasses; ++i) {
     if (kRowsPerPass * i >= nrows) break;
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, 4) qk_norm_rope_kv_write_kernel(cons
       *reinterpret_cast<Vec*>(a.v_pool + v_off + (hh - a.num_heads - a.num_kv_heads) * a.vp_h +
                               d) = raw[i];
     }
+  }
   }
 }
 
@@ -294,8 +298,7 @@ extern "C" int b200_qk_norm_rope_kv_write(
       if ((st & 3) != 0) return B200_ERR_ALIGNMENT;
   }
   const int heads = num_heads + (pool ? 2 : 1) * num_kv_heads;
-  const int64_t warps =
-      static_cast<int64_t>(batch) * n_tokens * ((heads + kRowsPerWarp - 1) / kRowsPerWarp);
+  const int64_t warps = static_cast<int64_t>(batch) * n_tokens;  // one warp per token
   if (warps > 0x7fffffff - kWarps) return B200_ERR_INVALID_ARGUMENT;
   const int64_t blocks = (warps + kWarps - 1) / kWarps;
 
