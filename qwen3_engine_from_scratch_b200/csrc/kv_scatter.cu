@@ -19,6 +19,7 @@
 namespace {
 
 constexpr int kChunksPerRow = 16;  // 128 bf16 = 256 bytes = 16 x 16 B
+constexpr int kThreadsPerRow = kChunksPerRow / 2;  // two 16-byte pieces per thread
 constexpr int kThreads = 256;
 
 B200_DEVICE uint4 ld_stream(const void* p) {
@@ -45,11 +46,30 @@ struct RowsArgs {
   int32_t* dev_status;
 };
 
+// Quotient and remainder of a non-negative position by the page size, in 32
+// bits whenever the position fits (64-bit division costs several times more).
+B200_DEVICE int64_t page_of(int64_t pos, int block_size, int64_t* off) {
+  if (pos <= 0x7fffffff) {
+    const int p = static_cast<int>(pos);
+    const int page = p / block_size;
+    *off = p - page * block_size;
+    return page;
+  }
+  const int64_t page = pos / block_size;
+  *off = pos - page * block_size;
+  return page;
+}
+
+// Each thread moves two 16-byte pieces of a row of K and of V (chunks c and
+// c + 8, so 8 consecutive threads cover a 128-byte line per access): half as
+// many threads pay the row's index arithmetic.  IdxT: int when the thread
+// count fits, else int64_t.
+template <typename IdxT>
 __global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArgs a) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const int chunk = static_cast<int>(idx & (kChunksPerRow - 1));
-  int64_t r = idx >> 4;  // (b, s, h) row index
-  const int64_t total = static_cast<int64_t>(a.batch) * a.n_tokens * a.num_kv_heads;
+  const IdxT idx = static_cast<IdxT>(blockIdx.x) * kThreads + threadIdx.x;
+  const int chunk = static_cast<int>(idx & (kThreadsPerRow - 1));
+  IdxT r = idx / kThreadsPerRow;  // (b, s, h) row index
+  const IdxT total = static_cast<IdxT>(a.batch) * a.n_tokens * a.num_kv_heads;
   if (r >= total) return;
   const int h = static_cast<int>(r % a.num_kv_heads);
   r /= a.num_kv_heads;
@@ -68,7 +88,8 @@ __global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArg
   } else {
     pos = a.start_pos + s;
   }
-  const int64_t page = pos / a.block_size;
+  int64_t off = 0;
+  const int64_t page = pos < 0 ? -1 : page_of(pos, a.block_size, &off);
   if (pos < 0 || page >= a.max_pages) {
     if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_SEQ_OVERFLOW);
     return;
@@ -78,15 +99,19 @@ __global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArg
     if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_PAGE);
     return;
   }
-  const int64_t off = pos - page * a.block_size;
   const int64_t e = static_cast<int64_t>(chunk) * 8;
-
-  const uint4 kv = ld_stream(a.k_new + b * a.kn_b + h * a.kn_h + s * a.kn_s + e);
-  const uint4 vv = ld_stream(a.v_new + b * a.vn_b + h * a.vn_h + s * a.vn_s + e);
-  *reinterpret_cast<uint4*>(a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
-                            off * a.kp_slot + e) = kv;
-  *reinterpret_cast<uint4*>(a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
-                            off * a.vp_slot + e) = vv;
+  const __nv_bfloat16* ks = a.k_new + b * a.kn_b + h * a.kn_h + s * a.kn_s + e;
+  const __nv_bfloat16* vs = a.v_new + b * a.vn_b + h * a.vn_h + s * a.vn_s + e;
+  const uint4 k0 = ld_stream(ks), k1 = ld_stream(ks + 64);
+  const uint4 v0 = ld_stream(vs), v1 = ld_stream(vs + 64);
+  __nv_bfloat16* kd = a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
+                      off * a.kp_slot + e;
+  __nv_bfloat16* vd = a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
+                      off * a.vp_slot + e;
+  *reinterpret_cast<uint4*>(kd) = k0;
+  *reinterpret_cast<uint4*>(kd + 64) = k1;
+  *reinterpret_cast<uint4*>(vd) = v0;
+  *reinterpret_cast<uint4*>(vd + 64) = v1;
 }
 
 struct SlotsArgs {
@@ -102,32 +127,53 @@ struct SlotsArgs {
   int32_t* dev_status;
 };
 
+template <typename IdxT>
 __global__ void __launch_bounds__(kThreads) kv_scatter_slots_kernel(const SlotsArgs a) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const int chunk = static_cast<int>(idx & (kChunksPerRow - 1));
-  int64_t r = idx >> 4;  // (t, h) row index
-  if (r >= static_cast<int64_t>(a.n_tokens) * a.num_kv_heads) return;
+  const IdxT idx = static_cast<IdxT>(blockIdx.x) * kThreads + threadIdx.x;
+  const int chunk = static_cast<int>(idx & (kThreadsPerRow - 1));
+  const IdxT r = idx / kThreadsPerRow;  // (t, h) row index
+  if (r >= static_cast<IdxT>(a.n_tokens) * a.num_kv_heads) return;
   const int h = static_cast<int>(r % a.num_kv_heads);
-  const int64_t t = r / a.num_kv_heads;
+  const IdxT t = r / a.num_kv_heads;
   const int64_t slot = a.slot_is_int64 ? static_cast<const int64_t*>(a.slots)[t]
                                        : static_cast<int64_t>(static_cast<const int32_t*>(a.slots)[t]);
   if (slot < 0) return;  // padding token
-  const int64_t phys = slot / a.block_size;
+  int64_t off = 0;
+  const int64_t phys = page_of(slot, a.block_size, &off);
   if (phys >= a.num_blocks) {
     if (chunk == 0) b200::flag_error(a.dev_status, B200_DEV_BAD_SLOT);
     return;
   }
-  const int64_t off = slot - phys * a.block_size;
   const int64_t e = static_cast<int64_t>(chunk) * 8;
-  const uint4 kv = ld_stream(a.k + t * a.k_t + h * a.k_h + e);
-  const uint4 vv = ld_stream(a.v + t * a.v_t + h * a.v_h + e);
-  *reinterpret_cast<uint4*>(a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
-                            off * a.kp_slot + e) = kv;
-  *reinterpret_cast<uint4*>(a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
-                            off * a.vp_slot + e) = vv;
+  const __nv_bfloat16* ks = a.k + t * a.k_t + h * a.k_h + e;
+  const __nv_bfloat16* vs = a.v + t * a.v_t + h * a.v_h + e;
+  const uint4 k0 = ld_stream(ks), k1 = ld_stream(ks + 64);
+  const uint4 v0 = ld_stream(vs), v1 = ld_stream(vs + 64);
+  __nv_bfloat16* kd = a.k_pool + phys * a.kp_blk + a.layer * a.kp_layer + h * a.kp_h +
+                      off * a.kp_slot + e;
+  __nv_bfloat16* vd = a.v_pool + phys * a.vp_blk + a.layer * a.vp_layer + h * a.vp_h +
+                      off * a.vp_slot + e;
+  *reinterpret_cast<uint4*>(kd) = k0;
+  *reinterpret_cast<uint4*>(kd + 64) = k1;
+  *reinterpret_cast<uint4*>(vd) = v0;
+  *reinterpret_cast<uint4*>(vd + 64) = v1;
 }
 
 bool mult8(int64_t s) { return (s & 7) == 0; }
+
+// rows / span mode over `rows` (token, kv head) rows
+int launch_rows(const RowsArgs& a, int64_t rows, void* stream) {
+  const int64_t threads = rows * kThreadsPerRow;
+  const int64_t blocks = (threads + kThreads - 1) / kThreads;
+  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
+  if (blocks * kThreads <= 0x7fffffff)
+    kv_scatter_rows_kernel<int><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(a);
+  else
+    kv_scatter_rows_kernel<int64_t><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                      static_cast<cudaStream_t>(stream)>>>(a);
+  return b200host::status_from_cuda(cudaGetLastError());
+}
 
 }  // namespace
 
@@ -175,12 +221,7 @@ extern "C" int b200_kv_scatter_rows(
   a.block_size = block_size; a.num_blocks = num_blocks; a.max_pages = max_pages;
   a.max_requests = max_requests; a.layer = layer; a.dev_status = dev_status;
 
-  const int64_t threads = static_cast<int64_t>(batch) * n_tokens * num_kv_heads * kChunksPerRow;
-  const int64_t blocks = (threads + kThreads - 1) / kThreads;
-  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  kv_scatter_rows_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
-                           static_cast<cudaStream_t>(stream)>>>(a);
-  return b200host::status_from_cuda(cudaGetLastError());
+  return launch_rows(a, static_cast<int64_t>(batch) * n_tokens * num_kv_heads, stream);
 }
 
 extern "C" int b200_kv_scatter_slots(
@@ -218,11 +259,15 @@ extern "C" int b200_kv_scatter_slots(
   a.n_tokens = n_tokens; a.num_kv_heads = num_kv_heads; a.block_size = block_size;
   a.num_blocks = num_blocks; a.layer = layer; a.dev_status = dev_status;
 
-  const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kChunksPerRow;
+  const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kThreadsPerRow;
   const int64_t blocks = (threads + kThreads - 1) / kThreads;
   if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  kv_scatter_slots_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
-                            static_cast<cudaStream_t>(stream)>>>(a);
+  if (blocks * kThreads <= 0x7fffffff)
+    kv_scatter_slots_kernel<int><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                   static_cast<cudaStream_t>(stream)>>>(a);
+  else
+    kv_scatter_slots_kernel<int64_t><<<static_cast<unsigned>(blocks), kThreads, 0,
+                                       static_cast<cudaStream_t>(stream)>>>(a);
   return b200host::status_from_cuda(cudaGetLastError());
 }
 
@@ -267,10 +312,5 @@ extern "C" int b200_kv_scatter_span(
   a.block_size = block_size; a.num_blocks = num_blocks; a.max_pages = num_pages;
   a.max_requests = 1; a.layer = layer; a.dev_status = dev_status;
 
-  const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kChunksPerRow;
-  const int64_t blocks = (threads + kThreads - 1) / kThreads;
-  if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  kv_scatter_rows_kernel<<<static_cast<unsigned>(blocks), kThreads, 0,
-                           static_cast<cudaStream_t>(stream)>>>(a);
-  return b200host::status_from_cuda(cudaGetLastError());
+  return launch_rows(a, static_cast<int64_t>(n_tokens) * num_kv_heads, stream);
 }
