@@ -824,9 +824,10 @@ def run_prefill(args, rank, world, local_rank, steps, warmup, headline=False):
                          "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4),
                          "peak_source": src, "traffic": read_traffic("varlen_prefill_kernel")},
-            "scatter": {"ms": round(s_ms, 4), "bytes": sbytes,
-                        "gbs": round(sbytes / (s_ms / 1e3) / 1e9, 1),
-                        "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "scatter": {"kernel": "kv_scatter_slots_kernel", "ms": round(s_ms, 4),
+                        "bytes": sbytes, "gbs": round(sbytes / (s_ms / 1e3) / 1e9, 1),
+                        "frac_hbm": round(sbytes / (s_ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                        "traffic": read_traffic("kv_scatter_slots_kernel")},
             "prologue": prologue,
             "paged_prefill": chunked,
             "gpu_launches_per_step": 2, **extra}
