@@ -501,10 +501,13 @@ __global__ void __launch_bounds__(kChunkThreads, 3) sample_chunk_kernel(const Sa
         for (int j2 = 0; j2 < cn; ++j2) r += c[j2] > v ? 1 : 0;
         if (r < k) dst[r] = v;
       }
-      for (int i = k + tid; i < k_sel; i += kChunkThreads) dst[i] = 0;
+      // slots past the ranked entries hold no candidate (key 0)
+      for (int i = min(cn, k) + tid; i < k_sel; i += kChunkThreads) dst[i] = 0;
       return;
     }
-    // a bound tied across many threads: the general search below
+    // a bound tied across many threads: the general search below, once every
+    // thread has read the count (the search resets it)
+    __syncthreads();
   }
   select_k<kChunkThreads, kChunkPer>(key, k, low, ident, c, red, &s_count);
   // sorted by (score desc, index asc): the row kernel then meets equal scores
@@ -632,13 +635,19 @@ __global__ void __launch_bounds__(kRowFastThreads) sample_row_fast_kernel(const 
   const int r = (k + a.chunks - 1) / a.chunks;
   const int ns = a.chunks * r;
   if (tid < ns) samp[tid] = src[(tid / r) * a.block_k + (tid % r)];
-  if (tid == 0) s_count = 0;
+  if (tid == 0) {
+    s_count = 0;
+    // a chunk shorter than r leaves empty slots (0) among the samples; if the
+    // k-th largest sample is one of those, no sample has rank k - 1 (the
+    // empty slots tie) and the bound stays 0: every candidate is taken
+    s_bound = 0;
+  }
   __syncthreads();
   if (tid < ns) {
     const uint64_t v = samp[tid];
     int rk = 0;
     for (int j = 0; j < ns; ++j) rk += samp[j] > v ? 1 : 0;
-    if (rk == k - 1) s_bound = v;
+    if (rk == k - 1 && v != 0) s_bound = v;
   }
   __syncthreads();
   const uint64_t bound = s_bound;

@@ -104,6 +104,27 @@ def test_small_k_ties_vs_oracle(cuda, native_lib):
     assert np.array_equal(out[:, 0].cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_ragged_last_chunk_ties_vs_oracle(dtype, cuda, native_lib):
+    """Vocabularies whose last 8192-logit chunk is short, with heavily tied
+    logits and k <= 64: the row kernel's samples then include empty slots of
+    the short chunk (the bound must fall back to taking every candidate), and
+    the full chunks' tied bounds take the block-wide search.  Several seeds
+    and rows, every token equal to the oracle's."""
+    import qwen3_engine_from_scratch_b200 as qb
+    g = torch.Generator(device=cuda).manual_seed(21)
+    for V in (2 * 8192 + 16, 8192 + 16, 3 * 8192 + 300):
+        logits = torch.randint(0, 7, (64, V), generator=g, device=cuda).float().to(dtype)
+        lf = logits.float().cpu().numpy()
+        for k, t, p, seed in ((64, 0.7, 0.9, 1), (64, 1.0, 1.0, 3), (50, 0.7, 0.9, 2),
+                              (33, 1.0, 1.0, 4)):
+            out = qb.sample_tokens(logits, t, k, p, seed=seed)
+            torch.cuda.synchronize()
+            want = osmp.sample_tokens(lf, t, k, p, seed)
+            got = out[:, 0].cpu().numpy()
+            assert np.array_equal(got, want), (V, k, seed, np.nonzero(got != want)[0][:8])
+
+
 def _tv(counts, probs):
     return 0.5 * np.abs(counts / counts.sum() - probs).sum()
 
