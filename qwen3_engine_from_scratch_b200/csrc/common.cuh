@@ -319,6 +319,15 @@ B200_DEVICE void st_global_v8(void* p, const uint32_t (&w)[8]) {
 B200_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 B200_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+// First statement of a kernel launched with b200host::launch_pdl: wait until
+// the previous kernel on the stream has completed and its writes are visible
+// (a no-op for an ordinary launch), then let the next programmatic dependent
+// start launching (it waits the same way before touching memory).
+B200_DEVICE void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace b200
 
 // ------------------------------------------------------------------ host side
@@ -337,5 +346,25 @@ int status_from_cuda(cudaError_t e);  // records e for b200_last_cuda_error_stri
 cudaError_t last_cuda_error();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch as a programmatic dependent of the previous kernel on the stream:
+// the grid may be scheduled while that kernel drains, which hides the launch
+// latency between back-to-back kernels.  The kernel must begin with
+// b200::pdl_begin() (nothing read or written before it).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
 
 }  // namespace b200host

@@ -66,6 +66,8 @@ B200_DEVICE int64_t page_of(int64_t pos, int block_size, int64_t* off) {
 // count fits, else int64_t.
 template <typename IdxT>
 __global__ void __launch_bounds__(kThreads) kv_scatter_rows_kernel(const RowsArgs a) {
+  // launched with b200host::launch_pdl: nothing read or written before this
+  b200::pdl_begin();
   const IdxT idx = static_cast<IdxT>(blockIdx.x) * kThreads + threadIdx.x;
   const int chunk = static_cast<int>(idx & (kThreadsPerRow - 1));
   IdxT r = idx / kThreadsPerRow;  // (b, s, h) row index
@@ -129,6 +131,8 @@ struct SlotsArgs {
 
 template <typename IdxT>
 __global__ void __launch_bounds__(kThreads) kv_scatter_slots_kernel(const SlotsArgs a) {
+  // launched with b200host::launch_pdl: nothing read or written before this
+  b200::pdl_begin();
   const IdxT idx = static_cast<IdxT>(blockIdx.x) * kThreads + threadIdx.x;
   const int chunk = static_cast<int>(idx & (kThreadsPerRow - 1));
   const IdxT r = idx / kThreadsPerRow;  // (t, h) row index
@@ -166,13 +170,12 @@ int launch_rows(const RowsArgs& a, int64_t rows, void* stream) {
   const int64_t threads = rows * kThreadsPerRow;
   const int64_t blocks = (threads + kThreads - 1) / kThreads;
   if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  if (blocks * kThreads <= 0x7fffffff)
-    kv_scatter_rows_kernel<int><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                  static_cast<cudaStream_t>(stream)>>>(a);
-  else
-    kv_scatter_rows_kernel<int64_t><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                      static_cast<cudaStream_t>(stream)>>>(a);
-  return b200host::status_from_cuda(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return b200host::status_from_cuda(
+      blocks * kThreads <= 0x7fffffff
+          ? b200host::launch_pdl(kv_scatter_rows_kernel<int>, grid, dim3(kThreads), 0, s, a)
+          : b200host::launch_pdl(kv_scatter_rows_kernel<int64_t>, grid, dim3(kThreads), 0, s, a));
 }
 
 }  // namespace
@@ -262,13 +265,12 @@ extern "C" int b200_kv_scatter_slots(
   const int64_t threads = static_cast<int64_t>(n_tokens) * num_kv_heads * kThreadsPerRow;
   const int64_t blocks = (threads + kThreads - 1) / kThreads;
   if (blocks > 0x7fffffff) return B200_ERR_INVALID_ARGUMENT;
-  if (blocks * kThreads <= 0x7fffffff)
-    kv_scatter_slots_kernel<int><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                   static_cast<cudaStream_t>(stream)>>>(a);
-  else
-    kv_scatter_slots_kernel<int64_t><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                       static_cast<cudaStream_t>(stream)>>>(a);
-  return b200host::status_from_cuda(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return b200host::status_from_cuda(
+      blocks * kThreads <= 0x7fffffff
+          ? b200host::launch_pdl(kv_scatter_slots_kernel<int>, grid, dim3(kThreads), 0, s, a)
+          : b200host::launch_pdl(kv_scatter_slots_kernel<int64_t>, grid, dim3(kThreads), 0, s, a));
 }
 
 extern "C" int b200_kv_scatter_span(

@@ -131,12 +131,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   __shared__ __align__(8) uint64_t bars[kWarps * kStages];
   __shared__ float s_ml[kWarps][kMaxG][2];
 
-  // Launched as a programmatic dependent of the previous kernel on the stream:
-  // nothing is read or written before that kernel has completed and its
-  // writes are visible (griddepcontrol.wait; a no-op for an ordinary launch).
-  // The next kernel may start launching once every CTA of this grid is running.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // launched with b200host::launch_pdl: nothing read or written before this
+  b200::pdl_begin();
 
   const int pair = blockIdx.x;
   const int split = blockIdx.y;
@@ -582,21 +578,10 @@ int launch_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const v
   if (st != B200_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(static_cast<unsigned>(batch * num_kv_heads), static_cast<unsigned>(ms));
-  // programmatic dependent launch: the CTAs of this grid may be scheduled
-  // while the previous kernel on the stream finishes (each waits for it in
-  // the kernel before touching memory), which hides the launch latency
-  // between back-to-back layers
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return b200host::status_from_cuda(cudaLaunchKernelEx(&cfg, paged_decode_split_kernel, kmap, vmap, a));
+  // a programmatic dependent launch: the next layer's CTAs are launched while
+  // this grid's last wave drains
+  return b200host::status_from_cuda(b200host::launch_pdl(
+      paged_decode_split_kernel, grid, dim3(kThreads), kSmemBytes, s, kmap, vmap, a));
 }
 
 }  // namespace

@@ -123,6 +123,8 @@ B200_DEVICE uint64_t bf2_to_f2(uint32_t w) {
 // flight.
 template <int VEC>
 __global__ void __launch_bounds__(kThreads, 4) qk_norm_rope_kv_write_kernel(const PrologueArgs a) {
+  // launched with b200host::launch_pdl: nothing read or written before this
+  b200::pdl_begin();
   constexpr int kLanesPerRow = kD / VEC;        // 16 or 32
   constexpr int kRowsPerPass = 32 / kLanesPerRow;
   constexpr int kPasses = kRowsPerWarp / kRowsPerPass;
@@ -368,11 +370,9 @@ extern "C" int b200_qk_norm_rope_kv_write(
           mult8(kp_stride_h) && mult8(kp_stride_slot) && mult8(vp_stride_blk) &&
           mult8(vp_stride_layer) && mult8(vp_stride_h) && mult8(vp_stride_slot);
   }
-  if (v16)
-    qk_norm_rope_kv_write_kernel<8><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                      static_cast<cudaStream_t>(stream)>>>(a);
-  else
-    qk_norm_rope_kv_write_kernel<4><<<static_cast<unsigned>(blocks), kThreads, 0,
-                                      static_cast<cudaStream_t>(stream)>>>(a);
-  return b200host::status_from_cuda(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return b200host::status_from_cuda(
+      v16 ? b200host::launch_pdl(qk_norm_rope_kv_write_kernel<8>, grid, dim3(kThreads), 0, s, a)
+          : b200host::launch_pdl(qk_norm_rope_kv_write_kernel<4>, grid, dim3(kThreads), 0, s, a));
 }
