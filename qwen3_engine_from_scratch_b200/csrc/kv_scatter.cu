@@ -1,7 +1,8 @@
 // KV-cache slot scatter: copy new K/V rows (head_dim bf16 = 256 bytes each)
-// into the paged pool.  HBM-bound byte movement; one thread moves one 16-byte
-// chunk of K and the matching chunk of V, so a warp writes two full 256-byte
-// rows of each tensor with 16-byte vector stores.
+// into the paged pool.  HBM-bound byte movement; eight threads share a row,
+// each moving chunks c and c + 8 (16 bytes each) of K and of V, so every
+// access of the eight is one fully used 128-byte line and a warp writes four
+// 256-byte rows of each tensor with 16-byte vector stores.
 //
 //   rows  mode: position = seq_lens[row_ids[b]] + s, page from the 2-D block
 //               table (update_kv_batch_kernel, qwen3/kernels/paged_attention.py:
