@@ -6,7 +6,11 @@
  * point: raw device pointers, element strides, sizes, a CUDA stream.  No torch
  * types cross this boundary.  All entry points only enqueue work on `stream`
  * (no host synchronisation, no allocation, grid sizes derived from shapes
- * only), so they can be captured in a CUDA graph.
+ * only), so they can be captured in a CUDA graph.  The decode, prologue and
+ * KV-scatter kernels are launched as programmatic dependents of the previous
+ * kernel on `stream` (their CTAs may be scheduled while it drains); each one
+ * waits for that kernel's completion before its first memory access, so the
+ * stream order callers see is that of an ordinary launch.
  *
  * Conventions
  *   - bf16 tensors are passed as `const void*` / `void*` (2-byte elements).
