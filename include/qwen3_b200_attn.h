@@ -61,6 +61,19 @@ const char* b200_status_string(int status);
  * calling thread (behind a B200_ERR_CUDA return). */
 const char* b200_last_cuda_error_string(void);
 
+/* Failure-detection self-test (no counterpart in the reference, whose Triton
+ * kernels have no bounded waits): launches one warp on `stream` that waits on
+ * an mbarrier nothing completes, through the same bounded wait every pipeline
+ * wait of the prefill kernel uses.  The wait gives up after `limit_ns`
+ * nanoseconds of device time (1 ns .. 10 s), or as soon as *dev_status already
+ * holds B200_DEV_TIMEOUT (how one timed-out CTA ends the rest of its grid),
+ * then ORs B200_DEV_TIMEOUT into *dev_status and writes 0 to *result (1 if the
+ * wait had completed).  The kernel returns normally: the CUDA context stays
+ * usable, and kernels that check the status word (the prefill) start no new
+ * work until the caller clears it. */
+int b200_selftest_bounded_wait(int32_t* dev_status, int32_t* result, uint64_t limit_ns,
+                               void* stream);
+
 /* ABI version of this library (major*100 + minor). */
 int b200_abi_version(void);
 

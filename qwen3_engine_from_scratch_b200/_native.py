@@ -50,6 +50,7 @@ SIGNATURES = {
     "b200_abi_version": (_I, []),
     "b200_last_cuda_error_string": (ctypes.c_char_p, []),
     "b200_device_sm_count": (_I, []),
+    "b200_selftest_bounded_wait": (_I, [_P, _P, ctypes.c_uint64, _P]),
     "b200_kv_scatter_rows": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                   _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                   _P, _P, _I64, _P,

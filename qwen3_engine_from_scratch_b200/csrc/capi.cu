@@ -64,7 +64,42 @@ cudaError_t last_cuda_error() { return g_last_cuda_error; }
 
 }  // namespace b200host
 
+namespace {
+
+// One warp waits on an mbarrier that nothing completes, through the bounded
+// wait every prefill pipeline wait uses: it gives up after limit_ns (or at
+// once when dev_status already records a timeout elsewhere in the grid) and
+// records B200_DEV_TIMEOUT, and the kernel returns normally.
+__global__ void bounded_wait_probe_kernel(int32_t* dev_status, int32_t* result,
+                                          uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = b200::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    b200::mbar_init(b, 1);
+    b200::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool completed = b200::mbar_wait_abortable(b, 0, dev_status, limit_ns);
+  if (threadIdx.x == 0) {
+    if (!completed) b200::flag_error(dev_status, B200_DEV_TIMEOUT);
+    result[0] = completed ? 1 : 0;
+  }
+}
+
+constexpr uint64_t kMaxProbeWaitNs = 10000000000ull;  // 10 s
+
+}  // namespace
+
 extern "C" {
+
+int b200_selftest_bounded_wait(int32_t* dev_status, int32_t* result, uint64_t limit_ns,
+                               void* stream) {
+  if (dev_status == nullptr || result == nullptr || limit_ns == 0 || limit_ns > kMaxProbeWaitNs)
+    return B200_ERR_INVALID_ARGUMENT;
+  bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(dev_status, result,
+                                                                             limit_ns);
+  return b200host::status_from_cuda(cudaGetLastError());
+}
 
 const char* b200_status_string(int status) {
   switch (status) {
