@@ -83,6 +83,57 @@ def test_gloo_world2_tp_gather_and_sharding():
     assert all(total == sum([300, 20, 4000, 128, 77, 1000]) for _, _, total in res)
 
 
+def _leaving_rank_worker(rank, world, port, q):
+    """Rank 1 takes one exchange, then leaves between steps (no collective in
+    flight); rank 0's next exchange has to end with an error, not hang."""
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+    from qwen3_engine_from_scratch_b200.dist import kv_head_tp_all_gather
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    local = torch.full((2, 8, 128), float(rank))
+    kv_head_tp_all_gather(local)                 # step 1: both ranks take part
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()                          # the message is out before the exit
+        os._exit(0)                              # leaves between steps
+    t0 = time.monotonic()
+    try:
+        kv_head_tp_all_gather(local)             # step 2: the peer is gone
+        q.put((rank, "no error", time.monotonic() - t0))
+    except Exception:  # noqa: BLE001 -- gloo reports the lost peer as a RuntimeError subclass
+        q.put((rank, "error", time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_gloo_peer_that_leaves_ends_the_next_exchange_with_an_error():
+    """Failure detection without a GPU: a rank that exits between steps makes
+    its peer's next KV-head all-gather raise within the process group's short
+    timeout (5 s here) instead of waiting forever."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung on the lost peer"
+    res = dict((r, (what, dt)) for r, what, dt in (q.get(timeout=10) for _ in procs))
+    assert res[1][0] == "left"
+    assert res[0][0] == "error", res
+    assert res[0][1] < 60.0, res
+
+
 @needs_reference
 def test_shim_binds_into_reference_modules(monkeypatch):
     monkeypatch.syspath_prepend(REFERENCE)
