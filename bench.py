@@ -344,11 +344,18 @@ def run_b200(args, rank, world, local_rank):
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new)
     e2e_steps = max(3, min(args.steps, 50))
 
-    # layer-pipelined copies: layer l's q/k/v go up on a copy stream while
-    # earlier layers compute, each layer's output goes down on a second copy
-    # stream, and the step ends only after the last output reached the host.
+    # layer-pipelined copies: the step's q/k/v go up on a copy stream in
+    # groups of layers 1, 1, 2, 4, 8, ... (each group lands while the layers
+    # before it compute, with far fewer copies and cross-stream waits than one
+    # group per layer: 2.635 -> 2.588 ms per C2 step), each layer's output
+    # goes down on a second copy stream, and the step ends only after the last
+    # output reached the host.
     cs_in, cs_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    ev_in = [torch.cuda.Event() for _ in range(layers)]
+    groups, lo, size = [], 0, 1
+    while lo < layers:
+        groups.append((lo, min(layers, lo + size)))
+        lo, size = lo + size, (size * 2 if lo > 0 else 1)
+    ev_in = {a: torch.cuda.Event() for a, _ in groups}
     ev_done = [torch.cuda.Event() for _ in range(layers)]
 
     def e2e_step():
@@ -356,13 +363,14 @@ def run_b200(args, rank, world, local_rank):
         cs_in.wait_stream(cur)          # after the previous step (and joins a capture)
         cs_out.wait_stream(cur)
         with torch.cuda.stream(cs_in):
-            for l in range(layers):
-                dq[l].copy_(hq[l], non_blocking=True)
-                dk[l].copy_(hk[l], non_blocking=True)
-                dv[l].copy_(hv[l], non_blocking=True)
-                ev_in[l].record(cs_in)
+            for a, b in groups:
+                dq[a:b].copy_(hq[a:b], non_blocking=True)
+                dk[a:b].copy_(hk[a:b], non_blocking=True)
+                dv[a:b].copy_(hv[a:b], non_blocking=True)
+                ev_in[a].record(cs_in)
         for l in range(layers):
-            cur.wait_event(ev_in[l])
+            if l in ev_in:
+                cur.wait_event(ev_in[l])
             o = qb.triton_paged_attention_decode_batch(dq[l], dk[l], dv[l], caches, l, scale, rows)
             ev_done[l].record(cur)
             cs_out.wait_event(ev_done[l])
@@ -482,8 +490,9 @@ def run_b200(args, rank, world, local_rank):
                 "d2h_bytes_per_step": d2h_bytes,
                 "api": "triton_paged_attention_decode_batch for every layer, the step captured in "
                        "a CUDA graph as the reference's GraphRunner serves decode; pinned host "
-                       "q/k/v in and outputs out inside the graph, per-layer copies on two copy "
-                       "streams overlapping the compute",
+                       "q/k/v in and outputs out inside the graph on two copy streams "
+                       "overlapping the compute (uploads in layer groups 1, 1, 2, 4, 8, 12, "
+                       "downloads per layer)",
                 "eager": {"value": round(total_bytes_per_step / (e2e_eager_ms / 1e3) / 1e9, 1),
                           "ms_per_step": round(e2e_eager_ms, 4),
                           "api": "the same calls issued from Python every step"}},
