@@ -38,6 +38,9 @@ def test_library_exports_every_header_symbol(native_lib):
     assert not missing, f"declared in include/ but not exported: {missing}"
     # and the ctypes table covers the same set
     assert set(_native.SIGNATURES) == set(header_symbols())
+    # no b200_* entry point is exported without a declaration in include/
+    undeclared = sorted(s for s in exported if s.startswith("b200_") and s not in header_symbols())
+    assert not undeclared, f"exported but not declared in include/: {undeclared}"
 
 
 def test_library_is_sm100a_only(native_lib):
